@@ -1,0 +1,160 @@
+/*
+ * spmlp.h — C ABI of the B200 (sm_100a) activation-sparse GPT-NeoX MLP kernels.
+ *
+ * The library (libspmlp.so) replaces, for CUDA tensors, the forward path of
+ *   GPTNeoXMLP.forward = dense_4h_to_h(act(dense_h_to_4h(m)))
+ * (transformers/models/gpt_neox/modeling_gpt_neox.py, class GPTNeoXMLP) with
+ * `act` one of the reference's gate modules
+ * (src/sparsity_research/sites.py:86-107, runs/063-2026-10-07-pythia14m-tile-specialized-kernel/tile_gate.py:9-33),
+ * and the reference's sparse consumer / vocabulary-head kernels
+ * (runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:138-157, runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.cu:79-118).
+ *
+ * Conventions shared by every entry point
+ *   - All tensors are device pointers, row-major and contiguous, 16-byte aligned.
+ *   - Activations and weights share one dtype: SPMLP_F16 or SPMLP_BF16.
+ *     Accumulation is fp32; each output is rounded once (bias added first),
+ *     matching torch.nn.Linear on CUDA.
+ *   - Weights use torch.nn.Linear's layout: [out_features, in_features].
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); kernels are
+ *     launched on it and nothing synchronises the host.
+ *   - Return value: 0 on success, a negative SPMLP_E* code for an argument
+ *     error (nothing launched), or a positive cudaError_t.  The message of the
+ *     last failure on the calling thread is returned by spmlp_last_error().
+ *   - No entry point allocates device memory except where stated.
+ *   - The kernels never trap: a device-side wait that does not finish within
+ *     2 s records a code in the per-device status word (spmlp_device_status)
+ *     and the kernel returns.
+ */
+#ifndef SPMLP_H_
+#define SPMLP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtypes */
+#define SPMLP_F16 0
+#define SPMLP_BF16 1
+
+/* gate operators applied to z = round(x W_in^T + b_in) (the `act` slot of GPTNeoXMLP) */
+#define SPMLP_GATE_IDENTITY 0    /* h = z                                                */
+#define SPMLP_GATE_GELU 1        /* h = gelu_erf(z): ungated A0 (ACT2FN["gelu"])          */
+#define SPMLP_GATE_ONE_SIDED 2   /* h = z if z >= kappa else 0: sites.py:86-94            */
+#define SPMLP_GATE_SYMMETRIC 3   /* h = z if |z| >= kappa else 0: sites.py:97-107         */
+#define SPMLP_GATE_RELU 4        /* h = max(z, 0): torch.nn.ReLU (sites.py:221-222)       */
+#define SPMLP_GATE_GELU_MASKED 5 /* h = gelu_erf(z) if z > kappa else 0                   */
+#define SPMLP_GATE_CORNER 6      /* 8x16 tile kept iff its top-left z > kappa: runs/063-2026-10-07-pythia14m-tile-specialized-kernel/tile_gate.py:20-33 */
+
+/* down-projection modes */
+#define SPMLP_DOWN_DENSE 0 /* every K-block multiplied (skipping disabled)          */
+#define SPMLP_DOWN_SKIP 1  /* K-blocks whose 16x64 tiles are all zero for the whole
+                              128-token tile are neither loaded nor multiplied      */
+
+/* error codes (negative returns) */
+#define SPMLP_EINVAL -1   /* bad argument (null pointer, bad enum, non-finite kappa) */
+#define SPMLP_ESHAPE -2   /* unsupported shape (alignment / divisibility)            */
+#define SPMLP_EALIGN -3   /* pointer not 16-byte aligned                              */
+#define SPMLP_EDEVICE -4  /* current device is not an sm_100 GPU                      */
+#define SPMLP_EDRIVER -5  /* tensor-map encoding unavailable or failed                */
+
+/* Tile bitmap geometry.  Bit (g % 32) of word [r * words + g / 32] is set iff
+ * the 16-token x 64-feature tile (rows 16r.., features 64g..) of h holds a
+ * nonzero.  words = spmlp_tile_bits_words(F); the buffer holds
+ * ceil(T/16) * words uint32 words. */
+int spmlp_tile_bits_words(int F);
+int64_t spmlp_tile_bits_size(int64_t T, int F);
+
+/* Tile bitmap of an existing h [T,F] (same bit semantics as spmlp_up_gate's;
+ * for callers whose h does not come from spmlp_up_gate).  Overwrites every
+ * word of tile_bits.  Requires F % 64 == 0.  No reference counterpart: the
+ * reference derives its K16 masks inside the consumer
+ * (runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:14-31). */
+int spmlp_tile_bits_from_h(const void* h, uint32_t* tile_bits, int64_t T, int F, int dtype, void* stream);
+
+/* Up-projection fused with bias, rounding, gate and tile bitmap.
+ * Replaces GPTNeoXMLP.dense_h_to_4h followed by GPTNeoXMLP.act
+ * (pythia.py:76-77 installs the gate as mlp.act).
+ *   x [T,d], w_in [F,d], b_in [F] (nullable) -> h [T,F], tile_bits (zeroed
+ *   here, then filled), z_out [T,F] (nullable: the pre-gate z, for checks).
+ *   kappa must already be rounded to the activation dtype (runs/063-2026-10-07-pythia14m-tile-specialized-kernel/kernel.py:17-19).
+ *   seq_len: tokens per sequence for SPMLP_GATE_CORNER (blocks restart per
+ *   sequence; seq_len % 8 == 0 or seq_len == T), ignored otherwise.
+ *   Requires d % 64 == 0, F % 64 == 0, 1 <= T < 2^31. */
+int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, uint32_t* tile_bits,
+                  void* z_out, int64_t T, int d, int F, int dtype, int gate_op, float kappa,
+                  int64_t seq_len, void* stream);
+
+/* Sparse down-projection.  Replaces GPTNeoXMLP.dense_4h_to_h and the h branch
+ * of the reference's joint consumer (runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:138-157,
+ * adapter call runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/candidate.py:26-33).
+ *   h [T,F], tile_bits from spmlp_up_gate (ignored for SPMLP_DOWN_DENSE),
+ *   w_out [d,F], b_out [d] (nullable), residual [T,d] (nullable) -> y [T,d]
+ *   y = round(h w_out^T + b_out), then round(y + residual) when given.
+ *   stats (nullable, 2 x uint64, accumulated): [0] issued K16 MMA steps,
+ *   [1] skipped K16 MMA steps, summed over 128-token x BN tiles.
+ *   Skipping is exact for finite weights (0 * w == 0). */
+int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_out, const void* b_out,
+                      const void* residual, void* y, int64_t T, int F, int d, int dtype, int mode,
+                      uint64_t* stats, void* stream);
+
+/* Whole gated MLP forward: spmlp_up_gate then spmlp_down_sparse, with the
+ * caller's h and tile-bit buffers as workspace (GPTNeoXMLP.forward). */
+int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const void* w_out,
+                      const void* b_out, const void* residual, void* y, void* h_workspace,
+                      uint32_t* bits_workspace, int64_t T, int d, int F, int dtype, int gate_op,
+                      float kappa, int64_t seq_len, int mode, uint64_t* stats, void* stream);
+
+/* head gate axes for spmlp_head_sparse */
+#define SPMLP_HEAD_DENSE 0  /* every K16 group and every vocabulary column                  */
+#define SPMLP_HEAD_GATE_K 1 /* skip 16x16 head-input tiles whose corner certificate failed  */
+#define SPMLP_HEAD_GATE_N 2 /* compute only the listed 128-column vocabulary tiles          */
+
+/* Corner certificates + cast of the vocabulary-head input.  Replaces the
+ * reference's prepare step (runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.cu:9-16,79-91;
+ * Head.forward at .../inference/head.py:64-79).
+ *   x [T,d] fp32 -> x_out [T,d] in dtype with dead 16x16 tiles zeroed, and
+ *   support bits: bit (j%32) of word [r*spmlp_head_support_words(d) + j/32]
+ *   set iff x[16r, 16j] > kappa (fp32 comparison before the cast).
+ *   Requires d % 64 == 0. */
+int spmlp_head_support_words(int d);
+int spmlp_head_prepare(const float* x, void* x_out, uint32_t* support, int64_t T, int d, int dtype,
+                       float kappa, void* stream);
+
+/* Vocabulary projection logits [T,V] = x [T,d] w_vocab[V,d]^T (embed_out, no
+ * bias), fp32 accumulation, one rounding to dtype.  Replaces Head.project /
+ * project_kernel (runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.cu:18-77,104-118).
+ *   gate_axis SPMLP_HEAD_DENSE: all columns.
+ *   SPMLP_HEAD_GATE_K: K16 steps whose 16x16 tile is dead for all 128 tokens
+ *     of a tile are skipped (support from spmlp_head_prepare).
+ *   SPMLP_HEAD_GATE_N: only the n_active 128-column tiles listed (device int32,
+ *     indices < ceil(V/128)) are computed; other logits are left unwritten
+ *     (spmlp_head_fill masks them).
+ *   stats (nullable): [0] issued K16 steps, [1] skipped K16 steps.
+ *   Requires d % 64 == 0, V % 128 == 0. */
+int spmlp_head_sparse(const void* x, const uint32_t* support, const void* w_vocab, void* logits,
+                      const int32_t* active_tiles, int n_active, int64_t T, int d, int V, int dtype,
+                      int gate_axis, uint64_t* stats, void* stream);
+
+/* Write `value` (rounded to dtype) into the listed 128-column tiles of logits [T,V]. */
+int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype,
+                    float value, void* stream);
+
+/* Status word of `device` written by kernels that gave up on a bounded wait
+ * (0 = none).  Reading synchronises that device.  clear resets it to 0. */
+int spmlp_device_status(int device, int* status_out);
+int spmlp_clear_device_status(int device);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* spmlp_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+int spmlp_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPMLP_H_ */

@@ -1,0 +1,85 @@
+"""ctypes binding of libspmlp.so (the C ABI declared in include/spmlp.h).
+
+Loading fails loudly: there is no CPU or PyTorch fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+from .build import LIB
+
+_c = ctypes
+VP = _c.c_void_p
+I64 = _c.c_int64
+I32 = _c.c_int
+F32 = _c.c_float
+
+# name -> (restype, argtypes); mirrors include/spmlp.h one to one.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "spmlp_version": (I32, []),
+    "spmlp_last_error": (_c.c_char_p, []),
+    "spmlp_tile_bits_words": (I32, [I32]),
+    "spmlp_tile_bits_size": (I64, [I64, I32]),
+    "spmlp_tile_bits_from_h": (I32, [VP, VP, I64, I32, I32, VP]),
+    "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
+    "spmlp_down_sparse": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
+    "spmlp_mlp_forward": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, I32, VP, VP]),
+    "spmlp_head_support_words": (I32, [I32]),
+    "spmlp_head_fill": (I32, [VP, VP, I32, I64, I32, I32, F32, VP]),
+    "spmlp_head_prepare": (I32, [VP, VP, VP, I64, I32, I32, F32, VP]),
+    "spmlp_head_sparse": (I32, [VP, VP, VP, VP, VP, I32, I64, I32, I32, I32, I32, VP, VP]),
+    "spmlp_device_status": (I32, [I32, _c.POINTER(I32)]),
+    "spmlp_clear_device_status": (I32, [I32]),
+}
+
+# Constants of include/spmlp.h.
+F16, BF16 = 0, 1
+GATE_IDENTITY, GATE_GELU, GATE_ONE_SIDED, GATE_SYMMETRIC, GATE_RELU, GATE_GELU_MASKED, GATE_CORNER = range(7)
+DOWN_DENSE, DOWN_SKIP = 0, 1
+HEAD_GATE_NONE, HEAD_GATE_K, HEAD_GATE_N = 0, 1, 2
+
+_lib: ctypes.CDLL | None = None
+
+
+class SpmlpError(RuntimeError):
+    """A libspmlp entry point returned a nonzero status."""
+
+    def __init__(self, name: str, code: int, message: str):
+        super().__init__(f"{name} failed with status {code}: {message}")
+        self.code = code
+
+
+def library_path() -> Path:
+    return LIB
+
+
+def load() -> ctypes.CDLL:
+    """Load libspmlp.so (built in-tree by ``__graft_entry__.build``)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB.exists():
+        raise RuntimeError(
+            f"{LIB} is missing: build it with `python -m sparsity_spillover_b200.build` "
+            "(there is no CPU fallback)"
+        )
+    lib = ctypes.CDLL(str(LIB))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point and raise SpmlpError on a nonzero status."""
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != 0:
+        raise SpmlpError(name, rc, lib.spmlp_last_error().decode(errors="replace"))
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)

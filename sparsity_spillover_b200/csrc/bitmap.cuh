@@ -1,0 +1,41 @@
+// Standalone 16x64 tile-bitmap builder for an existing activation h [T, F].
+//
+// spmlp_up_gate emits the bitmap as a by-product of its epilogue; this kernel
+// serves callers whose h comes from elsewhere (e.g. a tile-structured h fed
+// straight to the down-projection).  Bit semantics are the same: a tile's bit
+// is set iff one of its elements is nonzero (-0.0 counts as zero).
+#pragma once
+
+#include <stdint.h>
+
+namespace spmlp {
+
+// One CTA per 16-row group; each warp scans whole 16x64 tiles: lane l reads the
+// 64-byte half (l & 1) of row (l >> 1), i.e. four 16-byte vectors.
+__global__ void __launch_bounds__(256) tile_bits_kernel(const uint16_t* __restrict__ h, uint32_t* __restrict__ bits,
+                                                        int T, int F, int words) {
+  extern __shared__ uint32_t s_words[];
+  const int rg = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) s_words[w] = 0u;
+  __syncthreads();
+  const int tiles = F / 64;
+  const int row = rg * 16 + (lane >> 1);
+  for (int g = warp; g < tiles; g += nwarps) {
+    uint32_t acc = 0;
+    if (row < T) {
+      const uint4* p = reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * F + g * 64 + (lane & 1) * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = __ldcs(p + i);  // streamed once: do not keep in L1/L2
+        acc |= (v.x | v.y | v.z | v.w) & 0x7fff7fffu;
+      }
+    }
+    if (__any_sync(0xffffffffu, acc != 0) && lane == 0) atomicOr(&s_words[g >> 5], 1u << (g & 31));
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
+}
+
+}  // namespace spmlp

@@ -1,0 +1,615 @@
+// Persistent, warp-specialised sm_100a GEMM used by every kernel of the sparse
+// gated MLP:  C[M,N] = A[M,K] * B[N,K]^T  with both operands K-major fp16/bf16.
+//
+//   warp 0      TMA producer: walks the live K-blocks of each tile (bitmap
+//               driven, ballot/popc scheduled) and loads only those A/B tiles
+//               into a STAGES-deep shared-memory ring, so the ring holds the
+//               surviving tiles back to back (compaction through smem).
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128,
+//               N=BN, K=16) into a double-buffered TMEM accumulator.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (one token row per
+//               thread), apply the kind-specific epilogue and store.
+//
+// Kinds:
+//   KIND_UP    z = round(acc + b_in); h = gate(z); writes h, the 16x64 tile
+//              nonzero bitmap, and optionally z.      (GPTNeoXMLP.dense_h_to_4h + act)
+//   KIND_DOWN  y = round(acc + b_out) [then round(y + residual)], skipping
+//              K-blocks whose 16x64 tiles are all zero for the whole M-tile.
+//                                                     (GPTNeoXMLP.dense_4h_to_h)
+//   KIND_HEAD  logits = round(acc) over an explicit list of active 128-column
+//              vocabulary tiles, optionally skipping dead K16 groups of the
+//              head input (corner certificates).        (GPTNeoXForCausalLM.embed_out)
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sm100.cuh"
+
+namespace spmlp {
+
+enum Kind : int { KIND_UP = 0, KIND_DOWN = 1, KIND_HEAD = 2 };
+
+// Gate operators applied to the rounded up-projection output z.
+enum GateOp : int {
+  GATE_IDENTITY = 0,     // h = z
+  GATE_GELU = 1,         // h = gelu_erf(z)                         (A0, ungated GPT-NeoX)
+  GATE_ONE_SIDED = 2,    // h = z if z >= kappa else 0              (FixedOneSidedThreshold)
+  GATE_SYMMETRIC = 3,    // h = z if |z| >= kappa else 0            (FixedSymmetricThreshold)
+  GATE_RELU = 4,         // h = z if z > 0 else 0                   (torch.nn.ReLU)
+  GATE_GELU_MASKED = 5,  // h = gelu_erf(z) if z > kappa else 0     (gelu-then-mask variant)
+  GATE_CORNER = 6,       // 8x16 tile kept iff its top-left z > kappa (CornerTileThreshold)
+};
+
+constexpr int kBM = 128;       // tokens per tile (UMMA M)
+constexpr int kBK = 64;        // K elements per pipeline stage (one 128-byte swizzle row)
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kBitsRows = 16;  // bitmap tile height (tokens)
+constexpr int kBitsCols = 64;  // bitmap tile width (features)
+
+struct GemmParams {
+  int M, N, K;            // tokens, output columns, reduction length
+  int m_tiles, n_tiles;   // n_tiles = entries of col_tiles for KIND_HEAD
+  const void* bias;       // [N] in the activation dtype, nullable
+  void* out;              // [M, N] row-major output (h, y or logits)
+  void* z_out;            // KIND_UP: optional pre-gate z [M, N]
+  const void* residual;   // KIND_DOWN: optional [M, N]
+  uint32_t* bits_out;     // KIND_UP: 16x64 tile bitmap, zeroed by the host
+  const uint32_t* bits_in;  // KIND_DOWN: 16x64 bitmap; KIND_HEAD: 16x16 support bits
+  int bits_words;         // words per 16-row group in bits_out / bits_in
+  int skip;               // KIND_DOWN/HEAD: 1 = skip dead K granules
+  const int* col_tiles;   // KIND_HEAD: active BN-column tile indices
+  int gate_op;
+  float kappa;            // already rounded to the activation dtype
+  int seq_len;            // GATE_CORNER: tokens per sequence (blocks restart per sequence)
+  unsigned long long* stats;  // nullable: [0] issued K granules, [1] skipped K granules
+  int* status;            // device status word
+};
+
+template <bool BF16>
+struct DType;
+template <>
+struct DType<false> {
+  using T = __half;
+  __device__ static __forceinline__ uint16_t round_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+  __device__ static __forceinline__ float to_float(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+};
+template <>
+struct DType<true> {
+  using T = __nv_bfloat16;
+  __device__ static __forceinline__ uint16_t round_bits(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  }
+  __device__ static __forceinline__ float to_float(uint16_t b) { return __bfloat162float(__ushort_as_bfloat16(b)); }
+};
+
+__device__ __forceinline__ float gelu_erf(float z) { return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f)); }
+
+// Granule size of the K-skip bitmap for each kind (features per bit).
+template <int KIND>
+struct KGran {
+  static constexpr int value = (KIND == KIND_HEAD) ? 16 : kBitsCols;
+};
+
+// Live-K mask of one 32-granule chunk for M-tile m_blk.  Warp-collective: lane
+// j tests granule 32*chunk+j across the eight 16-row groups of the tile and
+// __ballot_sync gathers the answer.  Rows past the last row group are absent.
+__device__ __forceinline__ uint32_t live_chunk(const uint32_t* bits, int words, int row_groups, int m_blk,
+                                               int chunk, int granules, int lane) {
+  const int g = chunk * 32 + lane;
+  uint32_t live = 0;
+  if (g < granules) {
+    const int rg0 = m_blk * (kBM / kBitsRows);
+#pragma unroll
+    for (int r = 0; r < kBM / kBitsRows; ++r) {
+      const int rg = rg0 + r;
+      if (rg < row_groups) live |= (__ldg(bits + static_cast<size_t>(rg) * words + chunk) >> lane) & 1u;
+    }
+  }
+  return __ballot_sync(0xffffffffu, live != 0);
+}
+
+// Expand a granule mask (16-feature granules) to a 64-wide K-block mask.
+__device__ __forceinline__ uint32_t kblocks_of_k16(uint32_t m16) {
+  uint32_t kb = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if ((m16 >> (4 * i)) & 0xFu) kb |= 1u << i;
+  return kb;
+}
+
+template <int KIND, int BN, int STAGES, bool BF16>
+struct GemmTraits {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr uint32_t kBarrierBytes = 256;
+  static constexpr uint32_t kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 1024;  // +1 KiB for alignment
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(kTmemCols <= 512, "TMEM has 512 columns");
+};
+
+// Number of K granules (bitmap bits) in the reduction dimension.
+template <int KIND>
+__device__ __forceinline__ int k_granules(int K) {
+  return K / KGran<KIND>::value;
+}
+
+// Enumerate the live K-blocks (64-wide) of an M-tile, calling f(kb, k16_mask)
+// for each; k16_mask says which of the block's four K16 steps to issue.
+// Warp-collective (all 32 lanes must call it with the same arguments).
+template <int KIND, class F>
+__device__ __forceinline__ bool for_each_live_kblock(const GemmParams& p, int m_blk, int lane, F&& f) {
+  const int kblocks = p.K / kBK;
+  if (!p.skip || p.bits_in == nullptr) {
+    for (int kb = 0; kb < kblocks; ++kb)
+      if (!f(kb, 0xFu)) return false;
+    return true;
+  }
+  const int row_groups = (p.M + kBitsRows - 1) / kBitsRows;
+  const int granules = k_granules<KIND>(p.K);
+  const int chunks = (granules + 31) / 32;
+  for (int c = 0; c < chunks; ++c) {
+    const uint32_t mask = live_chunk(p.bits_in, p.bits_words, row_groups, m_blk, c, granules, lane);
+    if constexpr (KGran<KIND>::value == kBK) {
+      uint32_t pending = mask;
+      while (pending) {
+        const int kb = c * 32 + __ffs(pending) - 1;
+        pending &= pending - 1;
+        if (!f(kb, 0xFu)) return false;
+      }
+    } else {
+      // 16-feature granules: 32 granules = 8 K-blocks per chunk.
+      uint32_t pending = kblocks_of_k16(mask);
+      while (pending) {
+        const int i = __ffs(pending) - 1;
+        pending &= pending - 1;
+        if (!f(c * 8 + i, (mask >> (4 * i)) & 0xFu)) return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Count of live K-blocks and of live K16 steps of an M-tile (warp-collective).
+template <int KIND>
+__device__ __forceinline__ void count_live(const GemmParams& p, int m_blk, int lane, int& blocks, int& steps) {
+  blocks = 0;
+  steps = 0;
+  for_each_live_kblock<KIND>(p, m_blk, lane, [&](int, uint32_t k16) {
+    ++blocks;
+    steps += __popc(k16);
+    return true;
+  });
+}
+
+template <int KIND, int BN>
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_blk, int& n_col0) {
+  m_blk = t / p.n_tiles;
+  const int n_sel = t - m_blk * p.n_tiles;
+  if (KIND == KIND_HEAD && p.col_tiles != nullptr) {
+    n_col0 = __ldg(p.col_tiles + n_sel) * BN;
+  } else {
+    n_col0 = n_sel * BN;
+  }
+}
+
+// ------------------------------------------------------------------ epilogues
+// One call handles 32 accumulator columns of one token row.  `acc` holds fp32
+// bit patterns (all zero for a tile without live K-blocks).
+template <int KIND, bool BF16>
+struct Epilogue;
+
+template <bool BF16>
+struct Epilogue<KIND_UP, BF16> {
+  using D = DType<BF16>;
+  // Returns a 32-bit "nonzero h" flag for this row's 32 columns.
+  __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int lane, bool row_ok,
+                                               const uint32_t (&acc)[32]) {
+    uint16_t zb[32];
+    const uint16_t* bias = static_cast<const uint16_t*>(p.bias);
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float b[8];
+      if (bias != nullptr) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + col0 + j));
+        const uint16_t* rb = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = D::to_float(rb[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) zb[j + i] = D::round_bits(__uint_as_float(acc[j + i]) + b[i]);
+    }
+    uint16_t hb[32];
+    const float kappa = p.kappa;
+    switch (p.gate_op) {
+      case GATE_IDENTITY:
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j] = zb[j];
+        break;
+      case GATE_GELU:
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j] = D::round_bits(gelu_erf(D::to_float(zb[j])));
+        break;
+      case GATE_ONE_SIDED:
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j] = (D::to_float(zb[j]) < kappa) ? uint16_t(0) : zb[j];
+        break;
+      case GATE_SYMMETRIC:
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j] = (fabsf(D::to_float(zb[j])) < kappa) ? uint16_t(0) : zb[j];
+        break;
+      case GATE_RELU:
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j] = (D::to_float(zb[j]) > 0.f) ? zb[j] : uint16_t(0);
+        break;
+      case GATE_GELU_MASKED:
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          hb[j] = (D::to_float(zb[j]) > kappa) ? D::round_bits(gelu_erf(D::to_float(zb[j]))) : uint16_t(0);
+        break;
+      case GATE_CORNER: {
+        // Tiles are 8 tokens x 16 features; the corner row of this thread's
+        // block lives in lane (lane & ~7) of the same warp because blocks and
+        // warp row-quarters are both 8-aligned (host enforces seq_len % 8 == 0
+        // or a single sequence).  Columns 0 and 16 of the chunk are corners.
+        const int src = lane & ~7;
+        const uint32_t c0 = __shfl_sync(0xffffffffu, static_cast<uint32_t>(zb[0]), src);
+        const uint32_t c1 = __shfl_sync(0xffffffffu, static_cast<uint32_t>(zb[16]), src);
+        const bool keep0 = D::to_float(static_cast<uint16_t>(c0)) > kappa;
+        const bool keep1 = D::to_float(static_cast<uint16_t>(c1)) > kappa;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) hb[j] = keep0 ? zb[j] : uint16_t(0);
+#pragma unroll
+        for (int j = 16; j < 32; ++j) hb[j] = keep1 ? zb[j] : uint16_t(0);
+        break;
+      }
+      default:
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hb[j] = zb[j];
+        break;
+    }
+    bool nz = false;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) nz |= (hb[j] & 0x7fffu) != 0;  // -0.0 is a zero
+    if (row_ok) {
+      uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<size_t>(row) * p.N + col0;
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        w.x = uint32_t(hb[j + 0]) | (uint32_t(hb[j + 1]) << 16);
+        w.y = uint32_t(hb[j + 2]) | (uint32_t(hb[j + 3]) << 16);
+        w.z = uint32_t(hb[j + 4]) | (uint32_t(hb[j + 5]) << 16);
+        w.w = uint32_t(hb[j + 6]) | (uint32_t(hb[j + 7]) << 16);
+        *reinterpret_cast<uint4*>(out + j) = w;
+      }
+      if (p.z_out != nullptr) {
+        uint16_t* zo = static_cast<uint16_t*>(p.z_out) + static_cast<size_t>(row) * p.N + col0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 w;
+          w.x = uint32_t(zb[j + 0]) | (uint32_t(zb[j + 1]) << 16);
+          w.y = uint32_t(zb[j + 2]) | (uint32_t(zb[j + 3]) << 16);
+          w.z = uint32_t(zb[j + 4]) | (uint32_t(zb[j + 5]) << 16);
+          w.w = uint32_t(zb[j + 6]) | (uint32_t(zb[j + 7]) << 16);
+          *reinterpret_cast<uint4*>(zo + j) = w;
+        }
+      }
+    }
+    return nz && row_ok;
+  }
+};
+
+template <bool BF16>
+struct Epilogue<KIND_DOWN, BF16> {
+  using D = DType<BF16>;
+  __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int, bool row_ok,
+                                               const uint32_t (&acc)[32]) {
+    if (!row_ok) return false;
+    const uint16_t* bias = static_cast<const uint16_t*>(p.bias);
+    const uint16_t* res =
+        p.residual ? static_cast<const uint16_t*>(p.residual) + static_cast<size_t>(row) * p.N + col0 : nullptr;
+    uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<size_t>(row) * p.N + col0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float b[8];
+      if (bias != nullptr) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + col0 + j));
+        const uint16_t* rb = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = D::to_float(rb[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = 0.f;
+      }
+      uint16_t y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = D::round_bits(__uint_as_float(acc[j + i]) + b[i]);
+      if (res != nullptr) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(res + j);
+        const uint16_t* rr = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = D::round_bits(D::to_float(y[i]) + D::to_float(rr[i]));
+      }
+      uint4 w;
+      w.x = uint32_t(y[0]) | (uint32_t(y[1]) << 16);
+      w.y = uint32_t(y[2]) | (uint32_t(y[3]) << 16);
+      w.z = uint32_t(y[4]) | (uint32_t(y[5]) << 16);
+      w.w = uint32_t(y[6]) | (uint32_t(y[7]) << 16);
+      *reinterpret_cast<uint4*>(out + j) = w;
+    }
+    return false;
+  }
+};
+
+template <bool BF16>
+struct Epilogue<KIND_HEAD, BF16> {
+  using D = DType<BF16>;
+  __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int, bool row_ok,
+                                               const uint32_t (&acc)[32]) {
+    if (!row_ok) return false;
+    uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<size_t>(row) * p.N + col0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 w;
+      w.x = uint32_t(D::round_bits(__uint_as_float(acc[j + 0]))) |
+            (uint32_t(D::round_bits(__uint_as_float(acc[j + 1]))) << 16);
+      w.y = uint32_t(D::round_bits(__uint_as_float(acc[j + 2]))) |
+            (uint32_t(D::round_bits(__uint_as_float(acc[j + 3]))) << 16);
+      w.z = uint32_t(D::round_bits(__uint_as_float(acc[j + 4]))) |
+            (uint32_t(D::round_bits(__uint_as_float(acc[j + 5]))) << 16);
+      w.w = uint32_t(D::round_bits(__uint_as_float(acc[j + 6]))) |
+            (uint32_t(D::round_bits(__uint_as_float(acc[j + 7]))) << 16);
+      *reinterpret_cast<uint4*>(out + j) = w;
+    }
+    return false;
+  }
+};
+
+// ------------------------------------------------------------------ kernel
+template <int KIND, int BN, int STAGES, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                      const GemmParams p) {
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * Tr::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Tr::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* drain = acc_empty + 2;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_tiles = p.m_tiles * p.n_tiles;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4 * 32);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Tr::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    const uint64_t pol_b = l2_policy_evict_last();  // weights: reused by every tile
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      int m_blk, n_col0;
+      tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+      ok = for_each_live_kblock<KIND>(p, m_blk, lane, [&](int kb, uint32_t) {
+        bool good = true;
+        if (lane == 0) {
+          good = mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutProducer);
+          if (good) {
+            mbar_arrive_expect_tx(&full[stage], Tr::kStageBytes);
+            tma_load_2d(s_a + stage * Tr::kABytes, &tm_a, &full[stage], kb * kBK, m_blk * kBM, 0ull);
+            tma_load_2d(s_b + stage * Tr::kBBytes, &tm_b, &full[stage], kb * kBK, n_col0, pol_b);
+          }
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (good) {
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        return good;
+      });
+    }
+    if (!ok && lane == 0) {
+      // Error path: let the copies this warp started land before the CTA exits.
+      const int outstanding = issued < STAGES ? issued : STAGES;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < outstanding; ++i) {
+        if (--s < 0) {
+          s = STAGES - 1;
+          ph ^= 1u;
+        }
+        uint64_t start = global_timer_ns();
+        while (!mbar_try_wait(&full[s], ph)) {
+          if (global_timer_ns() - start > SPMLP_WAIT_NS) {
+            atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = umma_idesc_f16(kBM, BN, BF16);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    unsigned long long issued_steps = 0, skipped_steps = 0;
+    const int k_steps_total = p.K / 16;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      int m_blk, n_col0;
+      tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+      int live_blocks, live_steps;
+      count_live<KIND>(p, m_blk, lane, live_blocks, live_steps);
+      skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
+      issued_steps += static_cast<unsigned long long>(live_steps);
+      if (live_blocks == 0) continue;  // epilogue writes the zero-accumulator result itself
+      if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      uint32_t accumulate = 0;
+      ok = for_each_live_kblock<KIND>(p, m_blk, lane, [&](int, uint32_t k16) {
+        bool good = true;
+        if (lane == 0) {
+          good = mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma);
+          if (good) {
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(s_a + stage * Tr::kABytes);
+            const uint32_t b_addr = smem_u32(s_b + stage * Tr::kBBytes);
+            const uint64_t a_desc = sw128_kmajor_desc(a_addr);
+            const uint64_t b_desc = sw128_kmajor_desc(b_addr);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              if ((k16 >> k) & 1u) {
+                // +32 bytes per K16 step inside the 128-byte swizzled row (>>4 encoded)
+                umma_f16(d_tmem, a_desc + static_cast<uint64_t>(2 * k), b_desc + static_cast<uint64_t>(2 * k),
+                         idesc, accumulate);
+                accumulate = 1;
+              }
+            }
+            umma_commit(&empty[stage]);
+          }
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (good && ++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        return good;
+      });
+      if (!ok) break;
+      if (lane == 0) umma_commit(&acc_full[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) {
+      // Wait for every MMA this thread issued before TMEM is released.
+      umma_commit(drain);
+      uint64_t start = global_timer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (global_timer_ns() - start > SPMLP_WAIT_NS) {
+          atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
+          break;
+        }
+      }
+      if (p.stats != nullptr && KIND != KIND_UP) {
+        atomicAdd(p.stats + 0, issued_steps);
+        atomicAdd(p.stats + 1, skipped_steps);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      int m_blk, n_col0;
+      tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+      int live_blocks = 1, live_steps = 0;
+      if constexpr (KIND != KIND_UP) count_live<KIND>(p, m_blk, lane, live_blocks, live_steps);
+      const int row = m_blk * kBM + quarter * 32 + lane;
+      const bool row_ok = row < p.M;
+      const bool has_acc = live_blocks > 0;
+      if (has_acc) {
+        // Every lane observes the barrier itself before reading TMEM.
+        const bool good = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, p.status, kDevTimeoutEpilogue));
+        if (!good) break;
+        tc_fence_after();
+      }
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      uint32_t nz_bits = 0;  // KIND_UP: one bit per 64-column group of this tile
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        const int col0 = n_col0 + ch * 32;
+        uint32_t v[32];
+        if (has_acc) {
+          tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch * 32), v);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0u;
+        }
+        if (col0 >= p.N) continue;  // N is a multiple of 64; whole chunk out of range
+        const bool nz = Epilogue<KIND, BF16>::apply(p, row, col0, lane, row_ok, v);
+        if constexpr (KIND == KIND_UP) {
+          const uint32_t ball = __ballot_sync(0xffffffffu, nz);
+          const int grp = ch >> 1;  // 64-column group within the tile
+          if (ball & 0x0000ffffu) nz_bits |= 1u << (2 * grp);
+          if (ball & 0xffff0000u) nz_bits |= 1u << (2 * grp + 1);
+        }
+      }
+      if constexpr (KIND == KIND_UP) {
+        // Publish this tile's 16x64 bits: two 16-row groups per warp quarter.
+        if (lane == 0 && nz_bits != 0) {
+          const int g0 = n_col0 / kBitsCols;  // first 64-column group of the tile
+          const int word = g0 >> 5;
+          const int shift = g0 & 31;          // BN/64 <= 4 groups stay inside one word
+          for (int half = 0; half < 2; ++half) {
+            uint32_t w = 0;
+            for (int grp = 0; grp < BN / kBitsCols; ++grp)
+              if ((nz_bits >> (2 * grp + half)) & 1u) w |= 1u << (shift + grp);
+            const int rg = m_blk * (kBM / kBitsRows) + quarter * 2 + half;
+            if (w != 0) atomicOr(p.bits_out + static_cast<size_t>(rg) * p.bits_words + word, w);
+          }
+        }
+      }
+      if (has_acc) {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Tr::kTmemCols);
+  }
+}
+
+}  // namespace spmlp

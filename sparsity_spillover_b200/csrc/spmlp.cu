@@ -1,0 +1,444 @@
+// Host side of libspmlp.so: argument checks, TMA tensor maps, launches and the
+// extern "C" entry points declared in include/spmlp.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <algorithm>
+#include <mutex>
+#include <string>
+
+#include "gemm_sm100.cuh"
+#include "head_prepare.cuh"
+#include "bitmap.cuh"
+#include "spmlp.h"
+
+namespace spmlp {
+
+// One status word per device, written only by kernels that give up on a wait.
+__device__ int g_device_status = 0;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return static_cast<int>(e);
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int* status = nullptr;
+  bool ok = false;
+};
+
+std::mutex g_dev_mutex;
+DeviceInfo g_dev[kMaxDevices];
+
+int current_device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(SPMLP_EDEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  DeviceInfo& info = g_dev[dev];
+  if (!info.ok) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(SPMLP_EDEVICE, "device %d is sm_%d%d; libspmlp is built for sm_100a only", dev, major, minor);
+    e = cudaDeviceGetAttribute(&info.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_device_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status word)");
+    info.status = static_cast<int*>(addr);
+    info.ok = true;
+  }
+  *out = &info;
+  return 0;
+}
+
+// ---------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
+// K-major operand [rows, k] -> box of 64 (k) x box_rows, 128-byte swizzle.
+int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(SPMLP_EDRIVER, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPMLP_EDRIVER, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------- launch
+template <int KIND, int BN, int STAGES, bool BF16>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream, DeviceInfo* dev) {
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16>;
+  auto kernel = gemm_sm100_kernel<KIND, BN, STAGES, BF16>;
+  // Setting the attribute is per function; cheap and idempotent.
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  const int tiles = p.m_tiles * p.n_tiles;
+  if (tiles == 0) return 0;
+  const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
+  p.status = dev->status;
+  kernel<<<grid, kThreads, Tr::kSmemBytes, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return 0;
+}
+
+int check_dtype(int dtype) {
+  if (dtype != SPMLP_F16 && dtype != SPMLP_BF16) return fail(SPMLP_EINVAL, "dtype must be SPMLP_F16 or SPMLP_BF16");
+  return 0;
+}
+
+int check_gate(int gate_op, float kappa, int64_t T, int64_t seq_len) {
+  if (gate_op < SPMLP_GATE_IDENTITY || gate_op > SPMLP_GATE_CORNER) return fail(SPMLP_EINVAL, "unknown gate_op %d", gate_op);
+  const bool uses_kappa = gate_op == SPMLP_GATE_ONE_SIDED || gate_op == SPMLP_GATE_SYMMETRIC ||
+                          gate_op == SPMLP_GATE_GELU_MASKED || gate_op == SPMLP_GATE_CORNER;
+  if (uses_kappa && (!std::isfinite(kappa) || kappa < 0.f))
+    return fail(SPMLP_EINVAL, "kappa must be a finite nonnegative number");
+  if (gate_op == SPMLP_GATE_CORNER) {
+    if (seq_len <= 0) return fail(SPMLP_EINVAL, "corner gate needs seq_len > 0");
+    if (T % seq_len != 0) return fail(SPMLP_ESHAPE, "T=%lld is not a multiple of seq_len=%lld", (long long)T, (long long)seq_len);
+    if (seq_len != T && seq_len % 8 != 0)
+      return fail(SPMLP_ESHAPE, "corner gate with several sequences needs seq_len %% 8 == 0");
+  }
+  return 0;
+}
+
+int check_mk(int64_t T, int K, int N, const char* kname, const char* nname) {
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T=%lld must be in [1, 2^31)", (long long)T);
+  if (K < kBK || K % kBK != 0) return fail(SPMLP_ESHAPE, "%s=%d must be a positive multiple of 64", kname, K);
+  if (N < kBitsCols || N % kBitsCols != 0) return fail(SPMLP_ESHAPE, "%s=%d must be a positive multiple of 64", nname, N);
+  return 0;
+}
+
+}  // namespace
+
+int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uint32_t* bits, void* z_out, int64_t T,
+                 int d, int F, int dtype, int gate_op, float kappa, int64_t seq_len, cudaStream_t stream) {
+  int rc;
+  if (!x || !w_in || !h || !bits) return fail(SPMLP_EINVAL, "x, w_in, h and tile_bits must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if ((rc = check_mk(T, d, F, "d", "F"))) return rc;
+  if ((rc = check_gate(gate_op, kappa, T, seq_len))) return rc;
+  if (!aligned16(x) || !aligned16(w_in) || !aligned16(h) || (b_in && !aligned16(b_in)) || (z_out && !aligned16(z_out)))
+    return fail(SPMLP_EALIGN, "x, w_in, b_in, h and z_out must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const bool bf16 = dtype == SPMLP_BF16;
+  constexpr int BN = 256;
+  CUtensorMap ta, tb;
+  if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb, w_in, F, d, BN, bf16))) return rc;
+  const int words = spmlp_tile_bits_words(F);
+  const int64_t bits_size = spmlp_tile_bits_size(T, F);
+  cudaError_t e = cudaMemsetAsync(bits, 0, static_cast<size_t>(bits_size) * 4, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(tile_bits)");
+  GemmParams p{};
+  p.M = static_cast<int>(T);
+  p.N = F;
+  p.K = d;
+  p.m_tiles = static_cast<int>((T + kBM - 1) / kBM);
+  p.n_tiles = (F + BN - 1) / BN;
+  p.bias = b_in;
+  p.out = h;
+  p.z_out = z_out;
+  p.bits_out = bits;
+  p.bits_words = words;
+  p.gate_op = gate_op;
+  p.kappa = kappa;
+  p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : T);
+  if (bf16) return launch_gemm<KIND_UP, BN, 4, true>(ta, tb, p, stream, dev);
+  return launch_gemm<KIND_UP, BN, 4, false>(ta, tb, p, stream, dev);
+}
+
+int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void* b_out, const void* residual, void* y,
+              int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, cudaStream_t stream) {
+  int rc;
+  if (!h || !w_out || !y) return fail(SPMLP_EINVAL, "h, w_out and y must be non-null");
+  if (mode != SPMLP_DOWN_DENSE && mode != SPMLP_DOWN_SKIP) return fail(SPMLP_EINVAL, "unknown down mode %d", mode);
+  if (mode == SPMLP_DOWN_SKIP && !bits) return fail(SPMLP_EINVAL, "SPMLP_DOWN_SKIP needs tile_bits");
+  if ((rc = check_dtype(dtype))) return rc;
+  if ((rc = check_mk(T, F, d, "F", "d"))) return rc;
+  if (!aligned16(h) || !aligned16(w_out) || !aligned16(y) || (b_out && !aligned16(b_out)) ||
+      (residual && !aligned16(residual)))
+    return fail(SPMLP_EALIGN, "h, w_out, b_out, residual and y must be 16-byte aligned");
+  if (stats && (reinterpret_cast<uintptr_t>(stats) & 7u)) return fail(SPMLP_EALIGN, "stats must be 8-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const bool bf16 = dtype == SPMLP_BF16;
+  constexpr int BN = 256;
+  CUtensorMap ta, tb;
+  if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb, w_out, d, F, BN, bf16))) return rc;
+  GemmParams p{};
+  p.M = static_cast<int>(T);
+  p.N = d;
+  p.K = F;
+  p.m_tiles = static_cast<int>((T + kBM - 1) / kBM);
+  p.n_tiles = (d + BN - 1) / BN;
+  p.bias = b_out;
+  p.out = y;
+  p.residual = residual;
+  p.bits_in = bits;
+  p.bits_words = spmlp_tile_bits_words(F);
+  p.skip = mode == SPMLP_DOWN_SKIP ? 1 : 0;
+  p.stats = reinterpret_cast<unsigned long long*>(stats);
+  if (bf16) return launch_gemm<KIND_DOWN, BN, 4, true>(ta, tb, p, stream, dev);
+  return launch_gemm<KIND_DOWN, BN, 4, false>(ta, tb, p, stream, dev);
+}
+
+
+int tile_bits_impl(const void* h, uint32_t* bits, int64_t T, int F, int dtype, cudaStream_t stream) {
+  int rc;
+  if (!h || !bits) return fail(SPMLP_EINVAL, "h and tile_bits must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T must be in [1, 2^31)");
+  if (F < kBitsCols || F % kBitsCols) return fail(SPMLP_ESHAPE, "F=%d must be a positive multiple of 64", F);
+  if (!aligned16(h)) return fail(SPMLP_EALIGN, "h must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int words = spmlp_tile_bits_words(F);
+  const int groups = static_cast<int>((T + kBitsRows - 1) / kBitsRows);
+  tile_bits_kernel<<<groups, 256, static_cast<size_t>(words) * 4, stream>>>(static_cast<const uint16_t*>(h), bits,
+                                                                            static_cast<int>(T), F, words);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tile_bits_kernel launch");
+  return 0;
+}
+
+int head_prepare_impl(const float* x, void* x_out, uint32_t* support, int64_t T, int d, int dtype, float kappa,
+                      cudaStream_t stream) {
+  int rc;
+  if (!x || !x_out || !support) return fail(SPMLP_EINVAL, "x, x_out and support must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T must be in [1, 2^31)");
+  if (d < kBK || d % kBK) return fail(SPMLP_ESHAPE, "d=%d must be a positive multiple of 64", d);
+  if (!std::isfinite(kappa) || kappa < 0.f) return fail(SPMLP_EINVAL, "kappa must be a finite nonnegative number");
+  if (!aligned16(x) || !aligned16(x_out)) return fail(SPMLP_EALIGN, "x and x_out must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int words = spmlp_head_support_words(d);
+  const int groups = static_cast<int>((T + 15) / 16);
+  const size_t smem = static_cast<size_t>(words) * 4;
+  if (dtype == SPMLP_BF16)
+    head_prepare_kernel<true><<<groups, 256, smem, stream>>>(x, static_cast<uint16_t*>(x_out), support,
+                                                             static_cast<int>(T), d, words, kappa);
+  else
+    head_prepare_kernel<false><<<groups, 256, smem, stream>>>(x, static_cast<uint16_t*>(x_out), support,
+                                                              static_cast<int>(T), d, words, kappa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "head_prepare_kernel launch");
+  return 0;
+}
+
+int head_impl(const void* x, const uint32_t* support, const void* w, void* logits, const int32_t* active,
+              int n_active, int64_t T, int d, int V, int dtype, int gate_axis, uint64_t* stats,
+              cudaStream_t stream) {
+  int rc;
+  if (!x || !w || !logits) return fail(SPMLP_EINVAL, "x, w_vocab and logits must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if ((rc = check_mk(T, d, V, "d", "V"))) return rc;
+  if (V % 128 != 0) return fail(SPMLP_ESHAPE, "V=%d must be a multiple of 128", V);
+  if (gate_axis < SPMLP_HEAD_DENSE || gate_axis > SPMLP_HEAD_GATE_N)
+    return fail(SPMLP_EINVAL, "unknown gate_axis %d", gate_axis);
+  if (gate_axis == SPMLP_HEAD_GATE_K && !support) return fail(SPMLP_EINVAL, "SPMLP_HEAD_GATE_K needs support bits");
+  if (gate_axis == SPMLP_HEAD_GATE_N && (n_active < 0 || (n_active > 0 && !active)))
+    return fail(SPMLP_EINVAL, "SPMLP_HEAD_GATE_N needs a device list of n_active >= 0 tiles");
+  if (gate_axis == SPMLP_HEAD_GATE_N && n_active > V / 128)
+    return fail(SPMLP_EINVAL, "n_active=%d exceeds the %d vocabulary tiles", n_active, V / 128);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(logits)) return fail(SPMLP_EALIGN, "x, w_vocab and logits must be 16-byte aligned");
+  if (stats && (reinterpret_cast<uintptr_t>(stats) & 7u)) return fail(SPMLP_EALIGN, "stats must be 8-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const bool bf16 = dtype == SPMLP_BF16;
+  constexpr int BN = 128;
+  CUtensorMap ta, tb;
+  if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb, w, V, d, BN, bf16))) return rc;
+  GemmParams p{};
+  p.M = static_cast<int>(T);
+  p.N = V;
+  p.K = d;
+  p.m_tiles = static_cast<int>((T + kBM - 1) / kBM);
+  p.n_tiles = gate_axis == SPMLP_HEAD_GATE_N ? n_active : V / BN;
+  p.out = logits;
+  p.col_tiles = gate_axis == SPMLP_HEAD_GATE_N ? active : nullptr;
+  p.bits_in = gate_axis == SPMLP_HEAD_GATE_K ? support : nullptr;
+  p.bits_words = spmlp_head_support_words(d);
+  p.skip = gate_axis == SPMLP_HEAD_GATE_K ? 1 : 0;
+  p.stats = reinterpret_cast<unsigned long long*>(stats);
+  if (bf16) return launch_gemm<KIND_HEAD, BN, 6, true>(ta, tb, p, stream, dev);
+  return launch_gemm<KIND_HEAD, BN, 6, false>(ta, tb, p, stream, dev);
+}
+
+int head_fill_impl(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype, float value,
+                   cudaStream_t stream) {
+  int rc;
+  if (!logits || (n_tiles > 0 && !tiles)) return fail(SPMLP_EINVAL, "logits and tiles must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T must be in [1, 2^31)");
+  if (V < 128 || V % 128) return fail(SPMLP_ESHAPE, "V=%d must be a positive multiple of 128", V);
+  if (n_tiles < 0 || n_tiles > V / 128) return fail(SPMLP_EINVAL, "n_tiles=%d out of range", n_tiles);
+  if (!aligned16(logits)) return fail(SPMLP_EALIGN, "logits must be 16-byte aligned");
+  if (n_tiles == 0) return 0;
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  uint16_t bits;
+  if (dtype == SPMLP_BF16) {
+    __nv_bfloat16 b = __float2bfloat16_rn(value);
+    std::memcpy(&bits, &b, 2);
+  } else {
+    __half hv = __float2half_rn(value);
+    std::memcpy(&bits, &hv, 2);
+  }
+  const int row_blocks = static_cast<int>(std::min<int64_t>((T + 15) / 16, 4096));
+  dim3 grid(row_blocks, n_tiles);
+  head_fill_kernel<<<grid, 256, 0, stream>>>(static_cast<uint16_t*>(logits), tiles, n_tiles, static_cast<int>(T), V,
+                                             bits);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "head_fill_kernel launch");
+  return 0;
+}
+
+}  // namespace spmlp
+
+using namespace spmlp;
+
+extern "C" {
+
+int spmlp_version(void) { return 100; }
+
+const char* spmlp_last_error(void) { return g_last_error.c_str(); }
+
+int spmlp_tile_bits_words(int F) {
+  if (F <= 0) return 0;
+  const int groups = (F + kBitsCols - 1) / kBitsCols;
+  return (groups + 31) / 32;
+}
+
+int64_t spmlp_tile_bits_size(int64_t T, int F) {
+  if (T <= 0 || F <= 0) return 0;
+  return ((T + kBitsRows - 1) / kBitsRows) * static_cast<int64_t>(spmlp_tile_bits_words(F));
+}
+
+int spmlp_tile_bits_from_h(const void* h, uint32_t* tile_bits, int64_t T, int F, int dtype, void* stream) {
+  return tile_bits_impl(h, tile_bits, T, F, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, uint32_t* tile_bits, void* z_out,
+                  int64_t T, int d, int F, int dtype, int gate_op, float kappa, int64_t seq_len, void* stream) {
+  return up_gate_impl(x, w_in, b_in, h, tile_bits, z_out, T, d, F, dtype, gate_op, kappa, seq_len,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_out, const void* b_out,
+                      const void* residual, void* y, int64_t T, int F, int d, int dtype, int mode, uint64_t* stats,
+                      void* stream) {
+  return down_impl(h, tile_bits, w_out, b_out, residual, y, T, F, d, dtype, mode, stats,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const void* w_out, const void* b_out,
+                      const void* residual, void* y, void* h_workspace, uint32_t* bits_workspace, int64_t T, int d,
+                      int F, int dtype, int gate_op, float kappa, int64_t seq_len, int mode, uint64_t* stats,
+                      void* stream) {
+  int rc = up_gate_impl(x, w_in, b_in, h_workspace, bits_workspace, nullptr, T, d, F, dtype, gate_op, kappa, seq_len,
+                        static_cast<cudaStream_t>(stream));
+  if (rc) return rc;
+  return down_impl(h_workspace, bits_workspace, w_out, b_out, residual, y, T, F, d, dtype, mode, stats,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_head_support_words(int d) {
+  if (d <= 0) return 0;
+  return (d / 16 + 31) / 32;
+}
+
+int spmlp_head_prepare(const float* x, void* x_out, uint32_t* support, int64_t T, int d, int dtype, float kappa,
+                       void* stream) {
+  return head_prepare_impl(x, x_out, support, T, d, dtype, kappa, static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_head_sparse(const void* x, const uint32_t* support, const void* w_vocab, void* logits,
+                      const int32_t* active_tiles, int n_active, int64_t T, int d, int V, int dtype, int gate_axis,
+                      uint64_t* stats, void* stream) {
+  return head_impl(x, support, w_vocab, logits, active_tiles, n_active, T, d, V, dtype, gate_axis, stats,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype, float value,
+                    void* stream) {
+  return head_fill_impl(logits, tiles, n_tiles, T, V, dtype, value, static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_device_status(int device, int* status_out) {
+  if (!status_out) return fail(SPMLP_EINVAL, "status_out must be non-null");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status word)");
+  *status_out = v;
+  return 0;
+}
+
+int spmlp_clear_device_status(int device) {
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(status word)");
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,260 @@
+"""Tensor-level entry points over libspmlp.so, plus ``torch.ops.spmlp.*`` registrations.
+
+Each function mirrors the reference's kernel-adapter contract
+(runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:141-149 TORCH_CHECKs,
+candidate.py:26-33): CUDA tensors, contiguous, one device and dtype, launched on
+the caller's current stream, errors raised as exceptions.  Inference only.
+There is no CPU path: a tensor that is not on a CUDA device is an error.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .gates import OPERATORS, GateSpec, resolve
+
+_DTYPES = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check(name: str, t: torch.Tensor, dtype: torch.dtype | None, device: torch.device, shape=None) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} has dtype {t.dtype}, expected {dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def _device_dtype(x: torch.Tensor) -> tuple[torch.device, torch.dtype, int]:
+    if not x.is_cuda:
+        raise ValueError("libspmlp runs on CUDA tensors only (no CPU fallback)")
+    if x.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {x.dtype}; use float16 or bfloat16")
+    return x.device, x.dtype, _DTYPES[x.dtype]
+
+
+def tile_bits_size(tokens: int, features: int) -> int:
+    return int(_lib.load().spmlp_tile_bits_size(tokens, features))
+
+
+def tile_bits_words(features: int) -> int:
+    return int(_lib.load().spmlp_tile_bits_words(features))
+
+
+def tile_bits_from_h(h: torch.Tensor, bits: torch.Tensor | None = None) -> torch.Tensor:
+    """16x64 tile bitmap of an existing h [T,F] (int32 words, layout of include/spmlp.h)."""
+    device, dtype, code = _device_dtype(h)
+    _check("h", h, dtype, device)
+    t, f = h.shape
+    if bits is None:
+        bits = torch.empty((tile_bits_size(t, f),), device=device, dtype=torch.int32)
+    _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_tile_bits_from_h", _ptr(h), _ptr(bits), t, f, code, _stream(device))
+    return bits
+
+
+def up_gate(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, gate=None, *,
+            h: torch.Tensor | None = None, bits: torch.Tensor | None = None, z_out: torch.Tensor | None = None,
+            seq_len: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """h = gate(round(x w_in^T + b_in)) and the 16x64 tile bitmap of h.
+
+    x [T,d], w_in [F,d] (nn.Linear layout), b_in [F] or None.  ``gate`` is a
+    GateSpec, a reference gate spec mapping, a reference gate module, or None
+    (ungated A0: GELU).  z_out, when given, receives the pre-gate z.
+    """
+    device, dtype, code = _device_dtype(x)
+    spec: GateSpec = resolve(gate)
+    t, d = x.shape
+    f = w_in.shape[0]
+    _check("x", x, dtype, device)
+    _check("w_in", w_in, dtype, device, (f, d))
+    if b_in is not None:
+        _check("b_in", b_in, dtype, device, (f,))
+    if h is None:
+        h = torch.empty((t, f), device=device, dtype=dtype)
+    _check("h", h, dtype, device, (t, f))
+    if bits is None:
+        bits = torch.empty((tile_bits_size(t, f),), device=device, dtype=torch.int32)
+    _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    if z_out is not None:
+        _check("z_out", z_out, dtype, device, (t, f))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_up_gate", _ptr(x), _ptr(w_in), _ptr(b_in), _ptr(h), _ptr(bits), _ptr(z_out),
+                  t, d, f, code, spec.op, ctypes.c_float(spec.kappa_for(dtype)),
+                  int(seq_len or t), _stream(device))
+    return h, bits
+
+
+def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor, b_out: torch.Tensor | None,
+                residual: torch.Tensor | None = None, *, skip: bool = True, y: torch.Tensor | None = None,
+                stats: torch.Tensor | None = None) -> torch.Tensor:
+    """y = round(h w_out^T + b_out) [then round(y + residual)], skipping dead 16x64 K-tiles.
+
+    h [T,F], w_out [d,F], b_out [d] or None, residual [T,d] or None.
+    stats: optional int64[2] device tensor accumulating issued / skipped K16 steps.
+    """
+    device, dtype, code = _device_dtype(h)
+    t, f = h.shape
+    d = w_out.shape[0]
+    _check("h", h, dtype, device)
+    _check("w_out", w_out, dtype, device, (d, f))
+    if b_out is not None:
+        _check("b_out", b_out, dtype, device, (d,))
+    if residual is not None:
+        _check("residual", residual, dtype, device, (t, d))
+    if skip:
+        if bits is None:
+            raise ValueError("skip=True needs the tile bitmap")
+        _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    if y is None:
+        y = torch.empty((t, d), device=device, dtype=dtype)
+    _check("y", y, dtype, device, (t, d))
+    if stats is not None:
+        _check("stats", stats, torch.int64, device, (2,))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_down_sparse", _ptr(h), _ptr(bits) if skip else None, _ptr(w_out), _ptr(b_out),
+                  _ptr(residual), _ptr(y), t, f, d, code, _lib.DOWN_SKIP if skip else _lib.DOWN_DENSE,
+                  _ptr(stats), _stream(device))
+    return y
+
+
+def mlp_forward(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, w_out: torch.Tensor,
+                b_out: torch.Tensor | None, gate=None, *, residual: torch.Tensor | None = None, skip: bool = True,
+                h: torch.Tensor | None = None, bits: torch.Tensor | None = None, y: torch.Tensor | None = None,
+                stats: torch.Tensor | None = None, seq_len: int | None = None) -> torch.Tensor:
+    """GPTNeoXMLP.forward with a fused gate: both kernels, h/bits as reusable workspace."""
+    h, bits = up_gate(x, w_in, b_in, gate, h=h, bits=bits, seq_len=seq_len)
+    return down_sparse(h, bits, w_out, b_out, residual, skip=skip, y=y, stats=stats)
+
+
+def head_support_words(d: int) -> int:
+    return int(_lib.load().spmlp_head_support_words(d))
+
+
+def head_prepare(x: torch.Tensor, kappa: float, dtype: torch.dtype = torch.float16, *,
+                 x_out: torch.Tensor | None = None, support: torch.Tensor | None = None):
+    """fp32 head input -> (dtype input with dead 16x16 tiles zeroed, support bits).
+
+    kappa is compared in fp32 (float(torch.tensor(kappa, dtype=float32)),
+    runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.py:20-29).
+    """
+    if not x.is_cuda or x.dtype != torch.float32:
+        raise ValueError("head_prepare takes a CUDA float32 input")
+    if dtype not in _DTYPES:
+        raise ValueError("dtype must be float16 or bfloat16")
+    device = x.device
+    t, d = x.shape
+    _check("x", x, torch.float32, device)
+    words = head_support_words(d)
+    if x_out is None:
+        x_out = torch.empty((t, d), device=device, dtype=dtype)
+    _check("x_out", x_out, dtype, device, (t, d))
+    if support is None:
+        support = torch.empty(((t + 15) // 16) * words, device=device, dtype=torch.int32)
+    _check("support", support, torch.int32, device, (((t + 15) // 16) * words,))
+    k32 = float(torch.tensor(kappa, dtype=torch.float32))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_head_prepare", _ptr(x), _ptr(x_out), _ptr(support), t, d, _DTYPES[dtype],
+                  ctypes.c_float(k32), _stream(device))
+    return x_out, support
+
+
+def head_sparse(x: torch.Tensor, w_vocab: torch.Tensor, *, support: torch.Tensor | None = None,
+                active_tiles: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                stats: torch.Tensor | None = None) -> torch.Tensor:
+    """logits = x w_vocab^T (embed_out), optionally K-gated (support) or N-gated (active_tiles)."""
+    device, dtype, code = _device_dtype(x)
+    t, d = x.shape
+    v = w_vocab.shape[0]
+    _check("x", x, dtype, device)
+    _check("w_vocab", w_vocab, dtype, device, (v, d))
+    if support is not None and active_tiles is not None:
+        raise ValueError("give support (K gate) or active_tiles (N gate), not both")
+    axis = _lib.HEAD_GATE_NONE
+    n_active = 0
+    if support is not None:
+        axis = _lib.HEAD_GATE_K
+        _check("support", support, torch.int32, device, (((t + 15) // 16) * head_support_words(d),))
+    if active_tiles is not None:
+        axis = _lib.HEAD_GATE_N
+        _check("active_tiles", active_tiles, torch.int32, device)
+        n_active = active_tiles.numel()
+    if logits is None:
+        logits = torch.empty((t, v), device=device, dtype=dtype)
+    _check("logits", logits, dtype, device, (t, v))
+    if stats is not None:
+        _check("stats", stats, torch.int64, device, (2,))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_head_sparse", _ptr(x), _ptr(support), _ptr(w_vocab), _ptr(logits), _ptr(active_tiles),
+                  n_active, t, d, v, code, axis, _ptr(stats), _stream(device))
+    return logits
+
+
+def head_fill(logits: torch.Tensor, tiles: torch.Tensor, value: float) -> torch.Tensor:
+    """Write ``value`` into the listed 128-column vocabulary tiles of logits."""
+    device, dtype, code = _device_dtype(logits)
+    t, v = logits.shape
+    _check("logits", logits, dtype, device)
+    _check("tiles", tiles, torch.int32, device)
+    with torch.cuda.device(device):
+        _lib.call("spmlp_head_fill", _ptr(logits), _ptr(tiles), tiles.numel(), t, v, code, ctypes.c_float(value),
+                  _stream(device))
+    return logits
+
+
+def device_status(device: int | None = None) -> int:
+    """Status word written by kernels that gave up on a bounded wait (0 = none)."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    out = ctypes.c_int(0)
+    _lib.call("spmlp_device_status", dev, ctypes.byref(out))
+    return out.value
+
+
+def clear_device_status(device: int | None = None) -> None:
+    dev = torch.cuda.current_device() if device is None else int(device)
+    _lib.call("spmlp_clear_device_status", dev)
+
+
+# ---------------------------------------------------------------- torch.library ops
+# Functional custom ops so the kernels appear as torch.ops.spmlp.* (e.g. inside
+# user graphs); each allocates its outputs and calls the functions above.
+_LIB = torch.library.Library("spmlp", "DEF")
+_LIB.define("up_gate(Tensor x, Tensor w_in, Tensor? b_in, int gate_op, float kappa, int seq_len) -> (Tensor, Tensor)")
+_LIB.define("down_sparse(Tensor h, Tensor? bits, Tensor w_out, Tensor? b_out, Tensor? residual, bool skip) -> Tensor")
+_LIB.define("head_sparse(Tensor x, Tensor w_vocab, Tensor? support, Tensor? active_tiles) -> Tensor")
+
+_OP_NAMES = {v: k for k, v in OPERATORS.items()}
+
+
+def _up_gate_op(x, w_in, b_in, gate_op, kappa, seq_len):
+    op_name = _OP_NAMES[int(gate_op)]
+    spec = GateSpec(op_name, int(gate_op), float(kappa))
+    return up_gate(x, w_in, b_in, spec, seq_len=int(seq_len) or None)
+
+
+def _down_sparse_op(h, bits, w_out, b_out, residual, skip):
+    return down_sparse(h, bits, w_out, b_out, residual, skip=bool(skip))
+
+
+def _head_sparse_op(x, w_vocab, support, active_tiles):
+    return head_sparse(x, w_vocab, support=support, active_tiles=active_tiles)
+
+
+_LIB.impl("up_gate", _up_gate_op, "CUDA")
+_LIB.impl("down_sparse", _down_sparse_op, "CUDA")
+_LIB.impl("head_sparse", _head_sparse_op, "CUDA")
