@@ -1,0 +1,430 @@
+"""Benchmark of the B200 sparse gated MLP (driver contract: one JSON line on rank 0).
+
+Workload: Pythia-70M MLP, 6 stacked layers, d=512, F=2048,
+T=32768 tokens per GPU, fp16, one-sided threshold gate at 10% element density
+(kappa calibrated per layer by the kthvalue rule).  Layers are chained through
+the parallel residual, x_{l+1} = round(x_l + MLP_l(x_l)), which the down-projection
+kernel fuses.  One step = the 6-layer forward over one batch of tokens.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU: tokens are sharded (each rank owns a
+disjoint 32768-token batch, same weights), no collective on the data path; time
+is the max over ranks.  ``--impl reference`` times the reference's CPU path (the
+oracle restatement of GPTNeoXMLP + FixedOneSidedThreshold in fp32) on the host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "gated-MLP fwd tokens/s at 1/2/4/8 B200 and speedup vs dense GEMM by density"
+DENSITY = 0.10
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum),
+# summarised in profiles/; None until a capture of the current kernel exists.
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {"up_gate": None, "down_sparse": None}
+
+
+def peaks() -> tuple[dict, str]:
+    if PEAKS_FILE.exists():
+        return json.loads(PEAKS_FILE.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 100 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.proc = None
+        self.lines: list[str] = []
+        self._thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s, p in zip(sm, power) if p > 200] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_setup(backend: str):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+
+        kwargs = {"timeout": datetime.timedelta(seconds=120)}
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            kwargs["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(backend, **kwargs)
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int, device=None):
+    if world > 1:
+        import torch.distributed as dist
+
+        if device is not None:
+            dist.barrier(device_ids=[device.index])
+        else:
+            dist.barrier()
+
+
+# ---------------------------------------------------------------- our arm
+class Stack:
+    """Weights, calibrated gates and activation buffers of the 6-layer workload on one GPU."""
+
+    def __init__(self, device, rank: int, density: float):
+        import torch
+
+        from sparsity_spillover_b200 import ops, workloads
+
+        self.cfg = cfg = workloads.CONFIGS["cfg1"]
+        self.device = device
+        self.layers = workloads.make_weights(cfg, device)
+        self.x0 = workloads.make_input(cfg, device, token_offset=rank)
+        t, d, f = cfg.tokens, cfg.d, cfg.F
+        self.xs = [self.x0] + [torch.empty(t, d, dtype=cfg.dtype, device=device) for _ in range(cfg.layers)]
+        self.h = torch.empty(t, f, dtype=cfg.dtype, device=device)
+        self.bits = torch.empty(ops.tile_bits_size(t, f), dtype=torch.int32, device=device)
+        self.stats = torch.zeros(2, dtype=torch.int64, device=device)
+        self.gates = []
+        z = torch.empty(t, f, dtype=cfg.dtype, device=device)
+        for i, layer in enumerate(self.layers):
+            ops.up_gate(self.xs[i], layer.w_in, layer.b_in, {"operator": "identity"}, h=self.h, bits=self.bits,
+                        z_out=z)
+            kappa = workloads.quantile_threshold(z, density) if density < 1.0 else None
+            gate = {"operator": "one_sided_threshold", "kappa": kappa} if kappa is not None else {"operator": "identity"}
+            self.gates.append(gate)
+            self.layer(i, stats=self.stats)
+        del z
+        torch.cuda.synchronize(device)
+        self.density = self._density()
+
+    def _density(self) -> float:
+        # Element density of the last layer's h (calibration check).
+        return float((self.h != 0).float().mean())
+
+    def layer(self, i: int, stats=None, events=None):
+        from sparsity_spillover_b200 import ops
+
+        L = self.layers[i]
+        if events is not None:
+            events[0].record()
+        ops.up_gate(self.xs[i], L.w_in, L.b_in, self.gates[i], h=self.h, bits=self.bits)
+        if events is not None:
+            events[1].record()
+        ops.down_sparse(self.h, self.bits, L.w_out, L.b_out, self.xs[i], y=self.xs[i + 1], stats=stats)
+        if events is not None:
+            events[2].record()
+
+    def step(self, events=None):
+        for i in range(len(self.layers)):
+            self.layer(i, events=None if events is None else events[i])
+        return self.xs[-1]
+
+
+def dense_reference_step(stack: Stack):
+    """The same 6-layer forward as PyTorch runs it on CUDA: cuBLAS Linear, masked_fill gate, residual add."""
+    import torch
+
+    x = stack.x0
+    for layer, gate in zip(stack.layers, stack.gates):
+        z = torch.nn.functional.linear(x, layer.w_in, layer.b_in)
+        if gate["operator"] == "one_sided_threshold":
+            z = z.masked_fill(z < gate["kappa"], 0.0)
+        x = torch.nn.functional.linear(z, layer.w_out, layer.b_out) + x
+    return x
+
+
+def time_device(fn, steps: int, device) -> float:
+    import torch
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(stop) / 1e3 / steps
+
+
+def cpu_baseline(cfg, density: float, seconds: float = 12.0) -> dict:
+    """The reference's CPU path (oracle restatement, fp32) on a bounded token sample."""
+    import torch
+
+    from oracle import gates as og
+    from oracle import mlp as omlp
+    from sparsity_spillover_b200 import workloads
+
+    threads = torch.get_num_threads()
+    sample = 2048
+    layers = workloads.make_weights(cfg, "cpu", dtype=torch.float32)
+    x0 = workloads.make_input(cfg, "cpu", tokens=sample, dtype=torch.float32)
+    kappas = []
+    x = x0
+    with torch.inference_mode():
+        for L in layers:
+            z = omlp.linear(x, L.w_in, L.b_in)
+            k = max(0.0, og.kthvalue_threshold(z, density))
+            kappas.append(k)
+            x = omlp.mlp_forward_fp32(x, L.w_in, L.b_in, L.w_out, L.b_out, og.ONE_SIDED, k)[2] + x
+
+        def run():
+            xx = x0
+            for L, k in zip(layers, kappas):
+                xx = omlp.mlp_forward_fp32(xx, L.w_in, L.b_in, L.w_out, L.b_out, og.ONE_SIDED, k)[2] + xx
+            return xx
+
+        run()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or reps < 2:
+            run()
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+    return {"value": sample / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} tokens x {cfg.layers} layers fp32 (GPTNeoXMLP + FixedOneSidedThreshold restated, "
+                      f"torch CPU), {reps} reps in {dt * reps:.1f}s",
+            "cpu": _cpu_model(), "os_cpu_count": os.cpu_count()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_setup("nccl")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from sparsity_spillover_b200 import ops
+
+    with torch.inference_mode():
+        stack = Stack(device, rank, DENSITY)
+        cfg = stack.cfg
+        t, d, f, nl = cfg.tokens, cfg.d, cfg.F, cfg.layers
+        for _ in range(args.warmup):
+            stack.step()
+        torch.cuda.synchronize(device)
+
+        # ---- timed region: K steps, per-kernel events on the launching stream
+        ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(nl)] for _ in range(args.steps)]
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler(list(range(world)) if world > 1 else [local]) if rank == 0 else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        barrier(world, device)
+        torch.cuda.synchronize(device)
+        start.record()
+        for k in range(args.steps):
+            stack.step(events=ev[k])
+        stop.record()
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        clocks = sampler.stop() if sampler else None
+        elapsed = start.elapsed_time(stop) / 1e3
+        t_step = max_over_ranks(elapsed / args.steps, world, device)
+        t_up = statistics.fmean(e[0].elapsed_time(e[1]) for step in ev for e in step) / 1e3
+        t_dn = statistics.fmean(e[1].elapsed_time(e[2]) for step in ev for e in step) / 1e3
+        t_up = max_over_ranks(t_up, world, device)
+        t_dn = max_over_ranks(t_dn, world, device)
+
+        # ---- end to end through the public API: pinned host x -> device -> 6 layers -> host y
+        x_host = stack.x0.cpu().pin_memory()
+        y_host = torch.empty_like(x_host).pin_memory()
+
+        def e2e_step():
+            stack.xs[0].copy_(x_host, non_blocking=True)
+            y = stack.step()
+            y_host.copy_(y, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier(world, device)
+        t_e2e = max_over_ranks(time_device(e2e_step, args.steps, device), world, device)
+        stack.xs[0].copy_(stack.x0)
+
+        # ---- the same forward as stock PyTorch on CUDA (cuBLAS + masked_fill), for the ratio
+        for _ in range(2):
+            dense_reference_step(stack)
+        dense_ref_t = time_device(lambda: dense_reference_step(stack), max(3, args.steps // 2), device)
+        stats = stack.stats.cpu().tolist()
+        status = ops.device_status(local)
+
+    p, pk = peaks()
+    flop_up = 2.0 * t * d * f
+    flop_dn = 2.0 * t * d * f  # random element masks leave every 128x64 K-tile live; dense work is issued
+    dom = "up_gate" if t_up >= t_dn else "down_sparse"
+    t_dom = t_up if dom == "up_gate" else t_dn
+    peak_tf = p["bf16_tflops"]
+    achieved = (flop_up if dom == "up_gate" else flop_dn) / t_dom / 1e12
+    traffic = NCU_TRAFFIC_BYTES.get(dom)
+    # density-scaled algorithmic work of the whole step (f(ormula): L (2Tdf + 2Tdf rho))
+    ideal_flop = nl * (2.0 * t * d * f + 2.0 * t * d * f * DENSITY)
+    value = world * t / t_step
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded N(0,1) x, GPT-NeoX init weights)",
+        "config": {"workload": "cfg1: Pythia-70M gated MLP, 6 stacked layers, d=512 F=2048, T=32768/GPU, "
+                               "one-sided threshold gate at 10% element density, residual chained",
+                   "tokens_per_gpu": t, "layers": nl, "density_target": DENSITY,
+                   "density_measured": stack.density, "parallelism": f"token-sharded x{world}",
+                   "l2": "working set per step > L2 (h alone is 134 MB per layer)"},
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf, "traffic": traffic, "peak_source": f"{pk} bf16_tflops (burst)",
+                     "up_gate_us": t_up * 1e6, "down_sparse_us": t_dn * 1e6},
+        "density_scaled_roofline": {"algorithmic_tflop_per_step": ideal_flop / 1e12,
+                                    "achieved_tflops": ideal_flop / t_step / 1e12,
+                                    "frac": ideal_flop / t_step / 1e12 / peak_tf},
+        "skip_stats_calibration": {"issued_k16": stats[0], "skipped_k16": stats[1]},
+        "dense_pytorch_cuda": {"tokens_per_s": t / dense_ref_t, "speedup": dense_ref_t / (t_step)},
+        "e2e": {"value": world * t / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": t * d * 2,
+                "d2h_bytes_per_step": t * d * 2},
+        "gpu_launches": args.steps * nl * 2,
+        "clocks": clocks,
+        "device_status": status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from sparsity_spillover_b200 import workloads
+
+    cfg = workloads.CONFIGS["cfg1"]
+    torch.set_num_threads(os.cpu_count() or 1)
+    # Each step: the 6-layer fp32 CPU forward of a bounded token sample.
+    per_step_seconds = max(1.0, 60.0 / max(1, args.steps + args.warmup))
+    base = cpu_baseline(cfg, DENSITY, seconds=per_step_seconds)
+    value = base["value"]
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 2048 / value * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded N(0,1) x, GPT-NeoX init weights)",
+        "config": {"workload": "cfg1 sample: Pythia-70M gated MLP, 6 layers, d=512 F=2048, 2048-token sample, "
+                               "one-sided threshold gate at 10% density (reference CPU path, oracle port)"},
+        "impl": "reference",
+        "cpu_baseline": {"kind": base["kind"], "cores": base["cores"], "sample": base["sample"], "value": value,
+                         "unit": "tokens/s"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -7,8 +7,10 @@
 //               surviving tiles back to back (compaction through smem).
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128,
 //               N=BN, K=16) into a double-buffered TMEM accumulator.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (one token row per
-//               thread), apply the kind-specific epilogue and store.
+//   warps 2..   epilogue (4 or 8 warps): tcgen05.ld the accumulator (one
+//               token row per thread, software-pipelined), apply the
+//               kind-specific epilogue, stage 32x32 chunks in shared memory
+//               and write them with TMA bulk stores.
 //
 // Kinds:
 //   KIND_UP    z = round(acc + b_in); h = gate(z); writes h, the 16x64 tile
@@ -43,7 +45,6 @@ enum GateOp : int {
 
 constexpr int kBM = 128;       // tokens per tile (UMMA M)
 constexpr int kBK = 64;        // K elements per pipeline stage (one 128-byte swizzle row)
-constexpr int kThreads = 192;  // 6 warps
 constexpr int kBitsRows = 16;  // bitmap tile height (tokens)
 constexpr int kBitsCols = 64;  // bitmap tile width (features)
 
@@ -73,6 +74,17 @@ struct DType<false> {
   using T = __half;
   __device__ static __forceinline__ uint16_t round_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
   __device__ static __forceinline__ float to_float(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+  // Two fp32 values rounded (RN) into one packed word, low half first.
+  __device__ static __forceinline__ uint32_t pack_rn(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  __device__ static __forceinline__ __half2 h2(uint32_t w) { return *reinterpret_cast<const __half2*>(&w); }
+  // 0xFFFF in each half where a < b (false for NaN operands).
+  __device__ static __forceinline__ uint32_t lt_mask(uint32_t a, uint32_t b) { return __hlt2_mask(h2(a), h2(b)); }
+  __device__ static __forceinline__ uint32_t gt_mask(uint32_t a, uint32_t b) { return __hgt2_mask(h2(a), h2(b)); }
+  __device__ static __forceinline__ float lo(uint32_t w) { return to_float(static_cast<uint16_t>(w & 0xffffu)); }
+  __device__ static __forceinline__ float hi(uint32_t w) { return to_float(static_cast<uint16_t>(w >> 16)); }
 };
 template <>
 struct DType<true> {
@@ -81,6 +93,17 @@ struct DType<true> {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
   }
   __device__ static __forceinline__ float to_float(uint16_t b) { return __bfloat162float(__ushort_as_bfloat16(b)); }
+  __device__ static __forceinline__ uint32_t pack_rn(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  __device__ static __forceinline__ __nv_bfloat162 h2(uint32_t w) {
+    return *reinterpret_cast<const __nv_bfloat162*>(&w);
+  }
+  __device__ static __forceinline__ uint32_t lt_mask(uint32_t a, uint32_t b) { return __hlt2_mask(h2(a), h2(b)); }
+  __device__ static __forceinline__ uint32_t gt_mask(uint32_t a, uint32_t b) { return __hgt2_mask(h2(a), h2(b)); }
+  __device__ static __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
+  __device__ static __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 };
 
 __device__ __forceinline__ float gelu_erf(float z) { return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f)); }
@@ -118,16 +141,25 @@ __device__ __forceinline__ uint32_t kblocks_of_k16(uint32_t m16) {
   return kb;
 }
 
-template <int KIND, int BN, int STAGES, bool BF16>
+template <int KIND, int BN, int STAGES, bool BF16, int EPI = 4, int OUTBUF = 2>
 struct GemmTraits {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kEpiWarps = EPI;          // 4: one warp per TMEM lane quarter; 8: two, splitting columns
+  static constexpr int kThreads = 64 + 32 * EPI;
+  static constexpr uint32_t kStageOutBytes = 32 * 32 * 2;  // one 32-row x 32-column output chunk
+  static constexpr uint32_t kEpiBytes = EPI * OUTBUF * kStageOutBytes;  // OUTBUF staged chunks per warp
+  static constexpr uint32_t kBiasBytes = EPI * BN * 4;
   static constexpr uint32_t kBarrierBytes = 256;
-  static constexpr uint32_t kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 1024;  // +1 KiB for alignment
+  static constexpr uint32_t kSmemBytes =
+      STAGES * kStageBytes + kEpiBytes + kBiasBytes + kBarrierBytes + 1024;  // +1 KiB for alignment
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(EPI == 4 || EPI == 8, "4 or 8 epilogue warps");
+  static_assert(OUTBUF == 2 || OUTBUF == 4 || OUTBUF == 8, "2, 4 or 8 staging buffers per warp");
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB shared-memory limit");
 };
 
 // Number of K granules (bitmap bits) in the reduction dimension.
@@ -196,191 +228,109 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_b
 }
 
 // ------------------------------------------------------------------ epilogues
-// One call handles 32 accumulator columns of one token row.  `acc` holds fp32
-// bit patterns (all zero for a tile without live K-blocks).
-template <int KIND, bool BF16>
-struct Epilogue;
-
-template <bool BF16>
-struct Epilogue<KIND_UP, BF16> {
+// One call turns 32 accumulator columns of one token row into 16 packed output
+// words (32 fp16/bf16 values).  `acc` holds fp32 bit patterns (all zero for a
+// tile without live K-blocks); `bias` points at the 32 fp32 bias values of the
+// chunk in shared memory; `res` holds the chunk's 32 residual values.  The up
+// epilogue returns whether the row's 32 outputs hold a nonzero (bitmap).
+template <bool BF16, int GATE>
+struct UpEpilogue {
   using D = DType<BF16>;
-  // Returns a 32-bit "nonzero h" flag for this row's 32 columns.
+  // z = round(acc + b) two values per word; h = gate(z) computed on packed
+  // words: a comparison mask clears rejected halves (NaN compares false, so
+  // masked_fill(z < kappa, 0) keeps it, as torch does).
   __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int lane, bool row_ok,
-                                               const uint32_t (&acc)[32]) {
-    uint16_t zb[32];
-    const uint16_t* bias = static_cast<const uint16_t*>(p.bias);
+                                               const uint32_t (&acc)[32], const float* bias, uint32_t k2,
+                                               uint32_t (&out)[16]) {
+    uint32_t z[16];
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      float b[8];
-      if (bias != nullptr) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + col0 + j));
-        const uint16_t* rb = reinterpret_cast<const uint16_t*>(&raw);
+    for (int j = 0; j < 16; ++j)
+      z[j] = D::pack_rn(__uint_as_float(acc[2 * j]) + bias[2 * j], __uint_as_float(acc[2 * j + 1]) + bias[2 * j + 1]);
+    if constexpr (GATE == GATE_ONE_SIDED) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) b[i] = D::to_float(rb[i]);
-      } else {
+      for (int j = 0; j < 16; ++j) out[j] = z[j] & ~D::lt_mask(z[j], k2);
+    } else if constexpr (GATE == GATE_SYMMETRIC) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) b[i] = 0.f;
-      }
+      for (int j = 0; j < 16; ++j) out[j] = z[j] & ~D::lt_mask(z[j] & 0x7fff7fffu, k2);
+    } else if constexpr (GATE == GATE_RELU) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) zb[j + i] = D::round_bits(__uint_as_float(acc[j + i]) + b[i]);
+      for (int j = 0; j < 16; ++j) out[j] = z[j] & ~D::lt_mask(z[j], 0u);
+    } else if constexpr (GATE == GATE_GELU) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = D::pack_rn(gelu_erf(D::lo(z[j])), gelu_erf(D::hi(z[j])));
+    } else if constexpr (GATE == GATE_GELU_MASKED) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        out[j] = D::pack_rn(gelu_erf(D::lo(z[j])), gelu_erf(D::hi(z[j]))) & D::gt_mask(z[j], k2);
+    } else if constexpr (GATE == GATE_CORNER) {
+      // Tiles are 8 tokens x 16 features; the corner row of this thread's
+      // block lives in lane (lane & ~7) of the same warp because blocks and
+      // warp row-quarters are both 8-aligned (the host enforces seq_len % 8
+      // == 0 or a single sequence).  Columns 0 and 16 of the chunk are corners.
+      const int src = lane & ~7;
+      const uint32_t c0 = __shfl_sync(0xffffffffu, z[0], src);
+      const uint32_t c1 = __shfl_sync(0xffffffffu, z[8], src);
+      const uint32_t keep0 = D::lo(c0) > p.kappa ? 0xffffffffu : 0u;
+      const uint32_t keep1 = D::lo(c1) > p.kappa ? 0xffffffffu : 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = z[j] & keep0;
+#pragma unroll
+      for (int j = 8; j < 16; ++j) out[j] = z[j] & keep1;
+    } else {  // GATE_IDENTITY
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = z[j];
     }
-    uint16_t hb[32];
-    const float kappa = p.kappa;
-    switch (p.gate_op) {
-      case GATE_IDENTITY:
+    uint32_t any = 0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) hb[j] = zb[j];
-        break;
-      case GATE_GELU:
+    for (int j = 0; j < 16; ++j) any |= out[j];
+    if (p.z_out != nullptr && row_ok) {  // check/debug export of the pre-gate z
+      uint4* zo = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.z_out) + static_cast<size_t>(row) * p.N + col0);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) hb[j] = D::round_bits(gelu_erf(D::to_float(zb[j])));
-        break;
-      case GATE_ONE_SIDED:
-#pragma unroll
-        for (int j = 0; j < 32; ++j) hb[j] = (D::to_float(zb[j]) < kappa) ? uint16_t(0) : zb[j];
-        break;
-      case GATE_SYMMETRIC:
-#pragma unroll
-        for (int j = 0; j < 32; ++j) hb[j] = (fabsf(D::to_float(zb[j])) < kappa) ? uint16_t(0) : zb[j];
-        break;
-      case GATE_RELU:
-#pragma unroll
-        for (int j = 0; j < 32; ++j) hb[j] = (D::to_float(zb[j]) > 0.f) ? zb[j] : uint16_t(0);
-        break;
-      case GATE_GELU_MASKED:
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          hb[j] = (D::to_float(zb[j]) > kappa) ? D::round_bits(gelu_erf(D::to_float(zb[j]))) : uint16_t(0);
-        break;
-      case GATE_CORNER: {
-        // Tiles are 8 tokens x 16 features; the corner row of this thread's
-        // block lives in lane (lane & ~7) of the same warp because blocks and
-        // warp row-quarters are both 8-aligned (host enforces seq_len % 8 == 0
-        // or a single sequence).  Columns 0 and 16 of the chunk are corners.
-        const int src = lane & ~7;
-        const uint32_t c0 = __shfl_sync(0xffffffffu, static_cast<uint32_t>(zb[0]), src);
-        const uint32_t c1 = __shfl_sync(0xffffffffu, static_cast<uint32_t>(zb[16]), src);
-        const bool keep0 = D::to_float(static_cast<uint16_t>(c0)) > kappa;
-        const bool keep1 = D::to_float(static_cast<uint16_t>(c1)) > kappa;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) hb[j] = keep0 ? zb[j] : uint16_t(0);
-#pragma unroll
-        for (int j = 16; j < 32; ++j) hb[j] = keep1 ? zb[j] : uint16_t(0);
-        break;
-      }
-      default:
-#pragma unroll
-        for (int j = 0; j < 32; ++j) hb[j] = zb[j];
-        break;
+      for (int j = 0; j < 4; ++j) zo[j] = make_uint4(z[4 * j], z[4 * j + 1], z[4 * j + 2], z[4 * j + 3]);
     }
-    bool nz = false;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) nz |= (hb[j] & 0x7fffu) != 0;  // -0.0 is a zero
-    if (row_ok) {
-      uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<size_t>(row) * p.N + col0;
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 w;
-        w.x = uint32_t(hb[j + 0]) | (uint32_t(hb[j + 1]) << 16);
-        w.y = uint32_t(hb[j + 2]) | (uint32_t(hb[j + 3]) << 16);
-        w.z = uint32_t(hb[j + 4]) | (uint32_t(hb[j + 5]) << 16);
-        w.w = uint32_t(hb[j + 6]) | (uint32_t(hb[j + 7]) << 16);
-        *reinterpret_cast<uint4*>(out + j) = w;
-      }
-      if (p.z_out != nullptr) {
-        uint16_t* zo = static_cast<uint16_t*>(p.z_out) + static_cast<size_t>(row) * p.N + col0;
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 w;
-          w.x = uint32_t(zb[j + 0]) | (uint32_t(zb[j + 1]) << 16);
-          w.y = uint32_t(zb[j + 2]) | (uint32_t(zb[j + 3]) << 16);
-          w.z = uint32_t(zb[j + 4]) | (uint32_t(zb[j + 5]) << 16);
-          w.w = uint32_t(zb[j + 6]) | (uint32_t(zb[j + 7]) << 16);
-          *reinterpret_cast<uint4*>(zo + j) = w;
-        }
-      }
-    }
-    return nz && row_ok;
+    return row_ok && (any & 0x7fff7fffu) != 0;  // -0.0 is a zero
   }
 };
 
 template <bool BF16>
-struct Epilogue<KIND_DOWN, BF16> {
+struct DownEpilogue {
   using D = DType<BF16>;
-  __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int, bool row_ok,
-                                               const uint32_t (&acc)[32]) {
-    if (!row_ok) return false;
-    const uint16_t* bias = static_cast<const uint16_t*>(p.bias);
-    const uint16_t* res =
-        p.residual ? static_cast<const uint16_t*>(p.residual) + static_cast<size_t>(row) * p.N + col0 : nullptr;
-    uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<size_t>(row) * p.N + col0;
+  // y = round(acc + b); with a residual, round(y + r) computed in fp32 like torch's add.
+  __device__ __forceinline__ static void apply(const GemmParams& p, const uint32_t (&acc)[32], const float* bias,
+                                               const uint4 (&res)[4], uint32_t (&out)[16]) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      float b[8];
-      if (bias != nullptr) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(bias + col0 + j));
-        const uint16_t* rb = reinterpret_cast<const uint16_t*>(&raw);
+    for (int j = 0; j < 16; ++j)
+      out[j] = D::pack_rn(__uint_as_float(acc[2 * j]) + bias[2 * j], __uint_as_float(acc[2 * j + 1]) + bias[2 * j + 1]);
+    if (p.residual != nullptr) {
+      const uint32_t* r = reinterpret_cast<const uint32_t*>(&res[0]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) b[i] = D::to_float(rb[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) b[i] = 0.f;
-      }
-      uint16_t y[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = D::round_bits(__uint_as_float(acc[j + i]) + b[i]);
-      if (res != nullptr) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(res + j);
-        const uint16_t* rr = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = D::round_bits(D::to_float(y[i]) + D::to_float(rr[i]));
-      }
-      uint4 w;
-      w.x = uint32_t(y[0]) | (uint32_t(y[1]) << 16);
-      w.y = uint32_t(y[2]) | (uint32_t(y[3]) << 16);
-      w.z = uint32_t(y[4]) | (uint32_t(y[5]) << 16);
-      w.w = uint32_t(y[6]) | (uint32_t(y[7]) << 16);
-      *reinterpret_cast<uint4*>(out + j) = w;
+      for (int j = 0; j < 16; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(r[j]), D::hi(out[j]) + D::hi(r[j]));
     }
-    return false;
   }
 };
 
 template <bool BF16>
-struct Epilogue<KIND_HEAD, BF16> {
+struct HeadEpilogue {
   using D = DType<BF16>;
-  __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int, bool row_ok,
-                                               const uint32_t (&acc)[32]) {
-    if (!row_ok) return false;
-    uint16_t* out = static_cast<uint16_t*>(p.out) + static_cast<size_t>(row) * p.N + col0;
+  __device__ __forceinline__ static void apply(const uint32_t (&acc)[32], uint32_t (&out)[16]) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 w;
-      w.x = uint32_t(D::round_bits(__uint_as_float(acc[j + 0]))) |
-            (uint32_t(D::round_bits(__uint_as_float(acc[j + 1]))) << 16);
-      w.y = uint32_t(D::round_bits(__uint_as_float(acc[j + 2]))) |
-            (uint32_t(D::round_bits(__uint_as_float(acc[j + 3]))) << 16);
-      w.z = uint32_t(D::round_bits(__uint_as_float(acc[j + 4]))) |
-            (uint32_t(D::round_bits(__uint_as_float(acc[j + 5]))) << 16);
-      w.w = uint32_t(D::round_bits(__uint_as_float(acc[j + 6]))) |
-            (uint32_t(D::round_bits(__uint_as_float(acc[j + 7]))) << 16);
-      *reinterpret_cast<uint4*>(out + j) = w;
-    }
-    return false;
+    for (int j = 0; j < 16; ++j) out[j] = D::pack_rn(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1]));
   }
 };
 
 // ------------------------------------------------------------------ kernel
-template <int KIND, int BN, int STAGES, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int OUTBUF>
+__global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                      const GemmParams p) {
-  using Tr = GemmTraits<KIND, BN, STAGES, BF16>;
+                      const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + STAGES * Tr::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Tr::kStageBytes);
+  uint8_t* s_out = smem + STAGES * Tr::kStageBytes;  // [EPI][OUTBUF][32x32] staged output chunks
+  float* s_bias = reinterpret_cast<float*>(s_out + Tr::kEpiBytes);  // [EPI][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_bias) + Tr::kBiasBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
@@ -394,13 +344,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    tma_prefetch_desc(&tm_c);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4 * 32);
+      mbar_init(&acc_empty[i], EPI * 32);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -452,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           s = STAGES - 1;
           ph ^= 1u;
         }
-        uint64_t start = global_timer_ns();
+        const uint64_t start = global_timer_ns();
         while (!mbar_try_wait(&full[s], ph)) {
           if (global_timer_ns() - start > SPMLP_WAIT_NS) {
             atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
@@ -478,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       count_live<KIND>(p, m_blk, lane, live_blocks, live_steps);
       skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
       issued_steps += static_cast<unsigned long long>(live_steps);
-      if (live_blocks == 0) continue;  // epilogue writes the zero-accumulator result itself
+      if (live_blocks == 0) continue;  // the epilogue writes the zero-accumulator result itself
       if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
@@ -491,10 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           good = mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma);
           if (good) {
             tc_fence_after();
-            const uint32_t a_addr = smem_u32(s_a + stage * Tr::kABytes);
-            const uint32_t b_addr = smem_u32(s_b + stage * Tr::kBBytes);
-            const uint64_t a_desc = sw128_kmajor_desc(a_addr);
-            const uint64_t b_desc = sw128_kmajor_desc(b_addr);
+            const uint64_t a_desc = sw128_kmajor_desc(smem_u32(s_a + stage * Tr::kABytes));
+            const uint64_t b_desc = sw128_kmajor_desc(smem_u32(s_b + stage * Tr::kBBytes));
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k) {
               if ((k16 >> k) & 1u) {
@@ -525,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // Wait for every MMA this thread issued before TMEM is released.
       umma_commit(drain);
-      uint64_t start = global_timer_ns();
+      const uint64_t start = global_timer_ns();
       while (!mbar_try_wait(drain, 0)) {
         if (global_timer_ns() - start > SPMLP_WAIT_NS) {
           atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
@@ -538,48 +487,139 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5)
-    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    // ------------------------------------------------ epilogue warps
+    const int ew = warp - 2;               // 0 .. EPI-1
+    const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31 (hardware rule: warp id % 4)
+    constexpr int kChunks = BN / 32;
+    constexpr int kMyChunks = kChunks / (EPI / 4);
+    const int ch_begin = (ew / 4) * kMyChunks;  // EPI == 8: the two warps of a quarter split the columns
+    uint8_t* stage_out = s_out + ew * OUTBUF * Tr::kStageOutBytes;
+    float* bias_s = s_bias + ew * BN;
+    int out_buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
+    const uint32_t k2 = DType<BF16>::pack_rn(p.kappa, p.kappa);  // kappa in both halves (exact: pre-rounded)
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       int m_blk, n_col0;
       tile_coords<KIND, BN>(p, t, m_blk, n_col0);
       int live_blocks = 1, live_steps = 0;
       if constexpr (KIND != KIND_UP) count_live<KIND>(p, m_blk, lane, live_blocks, live_steps);
-      const int row = m_blk * kBM + quarter * 32 + lane;
+      const int row0 = m_blk * kBM + quarter * 32;
+      const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const bool has_acc = live_blocks > 0;
+
+      // Bias of this warp's columns -> shared memory (fp32), one 8-value vector per lane.
+      if constexpr (KIND != KIND_HEAD) {
+        __syncwarp();  // every lane is done with the previous tile's bias
+        for (int c = lane * 8; c < kMyChunks * 32; c += 256) {
+          const int col = n_col0 + ch_begin * 32 + c;
+          float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (p.bias != nullptr && col < p.N) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.bias) + col));
+            const uint16_t* rb = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) b[i] = DType<BF16>::to_float(rb[i]);
+          }
+          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + c)[0] = make_float4(b[0], b[1], b[2], b[3]);
+          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + c)[1] = make_float4(b[4], b[5], b[6], b[7]);
+        }
+        __syncwarp();
+      }
+
       if (has_acc) {
         // Every lane observes the barrier itself before reading TMEM.
         const bool good = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, p.status, kDevTimeoutEpilogue));
         if (!good) break;
         tc_fence_after();
       }
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      uint32_t nz_bits = 0;  // KIND_UP: one bit per 64-column group of this tile
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        const int col0 = n_col0 + ch * 32;
-        uint32_t v[32];
-        if (has_acc) {
-          tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch * 32), v);
-          tmem_wait_ld();
-        } else {
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+
+      // Residual prefetch (KIND_DOWN): 64 contiguous bytes of this row per chunk.
+      auto load_res = [&](int ch, uint4 (&r)[4]) {
+        if (KIND == KIND_DOWN && p.residual != nullptr && row_ok && n_col0 + ch * 32 < p.N) {
+          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.residual) +
+                                                            static_cast<size_t>(row) * p.N + n_col0 + ch * 32);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0u;
+          for (int i = 0; i < 4; ++i) r[i] = __ldg(src + i);
         }
-        if (col0 >= p.N) continue;  // N is a multiple of 64; whole chunk out of range
-        const bool nz = Epilogue<KIND, BF16>::apply(p, row, col0, lane, row_ok, v);
+      };
+
+      uint32_t nz_bits = 0;  // KIND_UP: bit (2*group + half) per 64-column group of the tile
+      auto process = [&](int ch, const uint32_t (&v)[32], const uint4 (&r)[4]) {
+        const int col0 = n_col0 + ch * 32;
+        if (col0 >= p.N) return;  // N is a multiple of 64: whole chunk out of range
+        uint32_t packed[16];
+        bool nz = false;
+        if constexpr (KIND == KIND_UP)
+          nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + ch * 32, k2, packed);
+        else if constexpr (KIND == KIND_DOWN)
+          DownEpilogue<BF16>::apply(p, v, bias_s + ch * 32, r, packed);
+        else
+          HeadEpilogue<BF16>::apply(v, packed);
         if constexpr (KIND == KIND_UP) {
           const uint32_t ball = __ballot_sync(0xffffffffu, nz);
-          const int grp = ch >> 1;  // 64-column group within the tile
+          const int grp = ch >> 1;
           if (ball & 0x0000ffffu) nz_bits |= 1u << (2 * grp);
           if (ball & 0xffff0000u) nz_bits |= 1u << (2 * grp + 1);
         }
+        // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) and hand it to TMA.
+        uint8_t* buf = stage_out + out_buf * Tr::kStageOutBytes;
+        if (lane == 0) bulk_wait_group_read<OUTBUF - 1>();  // the store that last used `buf` has read it
+        __syncwarp();
+        const int sw = (lane >> 1) & 3;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
+              make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < p.M) tma_store_2d(&tm_c, buf, col0, row0);
+          bulk_commit_group();
+        }
+        out_buf = (out_buf + 1) % OUTBUF;
+      };
+
+      uint32_t va[32], vb[32];
+      uint4 ra[4], rb[4];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) va[j] = vb[j] = 0u;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ra[i] = rb[i] = make_uint4(0u, 0u, 0u, 0u);
+      const int ch_end = ch_begin + kMyChunks;
+      if (has_acc) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch_begin * 32), va);
+      load_res(ch_begin, ra);
+#pragma unroll 1
+      for (int ch = ch_begin; ch < ch_end; ch += 2) {
+        // even chunk: va / ra
+        if (has_acc) {
+          tmem_wait_ld(va);
+          if (ch + 1 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 1) * 32), vb);
+          if (ch + 1 >= ch_end) {  // accumulator fully read: release it to the MMA warp
+            tc_fence_before();
+            mbar_arrive(&acc_empty[acc]);
+          }
+        }
+        if (ch + 1 < ch_end) load_res(ch + 1, rb);
+        process(ch, va, ra);
+        if (ch + 1 < ch_end) {
+          // odd chunk: vb / rb
+          if (has_acc) {
+            tmem_wait_ld(vb);
+            if (ch + 2 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 2) * 32), va);
+            if (ch + 2 >= ch_end) {
+              tc_fence_before();
+              mbar_arrive(&acc_empty[acc]);
+            }
+          }
+          if (ch + 2 < ch_end) load_res(ch + 2, ra);
+          process(ch + 1, vb, rb);
+        }
       }
       if constexpr (KIND == KIND_UP) {
-        // Publish this tile's 16x64 bits: two 16-row groups per warp quarter.
+        // Publish this warp's 16x64 bits: two 16-row groups per warp quarter.
         if (lane == 0 && nz_bits != 0) {
           const int g0 = n_col0 / kBitsCols;  // first 64-column group of the tile
           const int word = g0 >> 5;
@@ -593,15 +633,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (has_acc) {
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
-        }
+      if (has_acc && ++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA's shared memory goes away
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -42,6 +42,10 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 constexpr int kMaxDevices = 64;
 
+// Tile configuration of the up-projection: pipeline stages, epilogue warps,
+// staged output chunks per epilogue warp (tuned on B200 for d=512, F=2048).
+constexpr int kUpStages = 3, kUpEpiWarps = 4, kUpOutBufs = 4;
+
 struct DeviceInfo {
   int sm_count = 0;
   int* status = nullptr;
@@ -108,13 +112,29 @@ int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, 
   return 0;
 }
 
+// Row-major output [rows, cols] written in 32-row x 32-column boxes with 64-byte swizzle.
+int make_out_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(SPMLP_EDRIVER, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPMLP_EDRIVER, "cuTensorMapEncodeTiled (output) failed (CUresult %d)", static_cast<int>(r));
+  return 0;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- launch
-template <int KIND, int BN, int STAGES, bool BF16>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream, DeviceInfo* dev) {
-  using Tr = GemmTraits<KIND, BN, STAGES, BF16>;
-  auto kernel = gemm_sm100_kernel<KIND, BN, STAGES, BF16>;
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int OUTBUF>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
+                cudaStream_t stream, DeviceInfo* dev) {
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF>;
+  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, OUTBUF>;
   // Setting the attribute is per function; cheap and idempotent.
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
@@ -122,10 +142,33 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cuda
   if (tiles == 0) return 0;
   const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   p.status = dev->status;
-  kernel<<<grid, kThreads, Tr::kSmemBytes, stream>>>(ta, tb, p);
+  kernel<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(ta, tb, tc, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return 0;
+}
+
+// Up-projection launch with the gate operator as a compile-time parameter.
+template <int BN>
+int launch_up(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int gate_op,
+              bool bf16, cudaStream_t stream, DeviceInfo* dev) {
+  constexpr int S = kUpStages, E = kUpEpiWarps, B = kUpOutBufs;
+#define SPMLP_UP_CASE(G)                                                                   \
+  case G:                                                                                  \
+    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, B>(ta, tb, tc, p, stream, dev)   \
+                : launch_gemm<KIND_UP, G, BN, S, false, E, B>(ta, tb, tc, p, stream, dev);
+  switch (gate_op) {
+    SPMLP_UP_CASE(GATE_IDENTITY)
+    SPMLP_UP_CASE(GATE_GELU)
+    SPMLP_UP_CASE(GATE_ONE_SIDED)
+    SPMLP_UP_CASE(GATE_SYMMETRIC)
+    SPMLP_UP_CASE(GATE_RELU)
+    SPMLP_UP_CASE(GATE_GELU_MASKED)
+    SPMLP_UP_CASE(GATE_CORNER)
+    default:
+      return fail(SPMLP_EINVAL, "unknown gate_op %d", gate_op);
+  }
+#undef SPMLP_UP_CASE
 }
 
 int check_dtype(int dtype) {
@@ -173,6 +216,8 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
   if ((rc = make_kmajor_map(&tb, w_in, F, d, BN, bf16))) return rc;
+  CUtensorMap tc;
+  if ((rc = make_out_map(&tc, h, T, F, bf16))) return rc;
   const int words = spmlp_tile_bits_words(F);
   const int64_t bits_size = spmlp_tile_bits_size(T, F);
   cudaError_t e = cudaMemsetAsync(bits, 0, static_cast<size_t>(bits_size) * 4, stream);
@@ -191,8 +236,7 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   p.gate_op = gate_op;
   p.kappa = kappa;
   p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : T);
-  if (bf16) return launch_gemm<KIND_UP, BN, 4, true>(ta, tb, p, stream, dev);
-  return launch_gemm<KIND_UP, BN, 4, false>(ta, tb, p, stream, dev);
+  return launch_up<BN>(ta, tb, tc, p, gate_op, bf16, stream, dev);
 }
 
 int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void* b_out, const void* residual, void* y,
@@ -214,6 +258,8 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
   if ((rc = make_kmajor_map(&tb, w_out, d, F, BN, bf16))) return rc;
+  CUtensorMap tc;
+  if ((rc = make_out_map(&tc, y, T, d, bf16))) return rc;
   GemmParams p{};
   p.M = static_cast<int>(T);
   p.N = d;
@@ -227,8 +273,8 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   p.bits_words = spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_SKIP ? 1 : 0;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  if (bf16) return launch_gemm<KIND_DOWN, BN, 4, true>(ta, tb, p, stream, dev);
-  return launch_gemm<KIND_DOWN, BN, 4, false>(ta, tb, p, stream, dev);
+  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, 4, true, 4, 2>(ta, tb, tc, p, stream, dev);
+  return launch_gemm<KIND_DOWN, 0, BN, 4, false, 4, 2>(ta, tb, tc, p, stream, dev);
 }
 
 
@@ -299,6 +345,8 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
   if ((rc = make_kmajor_map(&tb, w, V, d, BN, bf16))) return rc;
+  CUtensorMap tc;
+  if ((rc = make_out_map(&tc, logits, T, V, bf16))) return rc;
   GemmParams p{};
   p.M = static_cast<int>(T);
   p.N = V;
@@ -311,8 +359,8 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   p.bits_words = spmlp_head_support_words(d);
   p.skip = gate_axis == SPMLP_HEAD_GATE_K ? 1 : 0;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  if (bf16) return launch_gemm<KIND_HEAD, BN, 6, true>(ta, tb, p, stream, dev);
-  return launch_gemm<KIND_HEAD, BN, 6, false>(ta, tb, p, stream, dev);
+  if (bf16) return launch_gemm<KIND_HEAD, 0, BN, 6, true, 4, 2>(ta, tb, tc, p, stream, dev);
+  return launch_gemm<KIND_HEAD, 0, BN, 6, false, 4, 2>(ta, tb, tc, p, stream, dev);
 }
 
 int head_fill_impl(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype, float value,
