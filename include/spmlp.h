@@ -107,6 +107,35 @@ int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const v
                       uint32_t* bits_workspace, int64_t T, int d, int F, int dtype, int gate_op,
                       float kappa, int64_t seq_len, int mode, uint64_t* stats, void* stream);
 
+/* Allocation-free variant of spmlp_mlp_forward.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory at the
+ * point of the call, for example code running while a stream is being captured
+ * into a CUDA graph (cudaMalloc is not permitted during a global-mode capture),
+ * code inside a framework or serving engine whose own allocator already holds
+ * the GPU's memory (a raw cudaMalloc can fail there, and cudaFree synchronises
+ * the device), or a foreign-language host with no binding to a device
+ * allocator.  Such callers pass only inputs and outputs.
+ *
+ * The workspace (h and the tile bitmap) lives in one static device buffer of
+ * SPMLP_NOALLOC_SCRATCH_BYTES inside the library, reserved on every GPU where
+ * the library's module is loaded and held until the process exits; the call
+ * itself allocates nothing.  Calls with 2*T*F (rounded up to 256) plus
+ * 4*spmlp_tile_bits_size(T, F) bytes above that size are rejected with
+ * SPMLP_ESHAPE: at F = 2048 that is about 8190 tokens per call.
+ *
+ * The first call on each device looks up the buffer's device address
+ * (cudaGetSymbolAddress with that device current) and caches it; make that
+ * first call before any stream capture.  Every call on a device shares the one
+ * buffer, which keeps the last call's contents (the bitmap is cleared on each
+ * call): calls that can overlap on the GPU — on different streams or from
+ * different host threads, on the same device — race on it and must be
+ * serialised by the caller.  Arguments and results are as spmlp_mlp_forward's. */
+#define SPMLP_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+int spmlp_mlp_forward_noalloc(const void* x, const void* w_in, const void* b_in, const void* w_out,
+                              const void* b_out, const void* residual, void* y, int64_t T, int d, int F,
+                              int dtype, int gate_op, float kappa, int64_t seq_len, int mode,
+                              uint64_t* stats, void* stream);
+
 /* head gate axes for spmlp_head_sparse */
 #define SPMLP_HEAD_DENSE 0  /* every K16 group and every vocabulary column                  */
 #define SPMLP_HEAD_GATE_K 1 /* skip 16x16 head-input tiles whose corner certificate failed  */

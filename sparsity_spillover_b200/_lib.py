@@ -25,6 +25,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
     "spmlp_down_sparse": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_mlp_forward": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, I32, VP, VP]),
+    "spmlp_mlp_forward_noalloc": (I32, [VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, I32, VP, VP]),
     "spmlp_head_support_words": (I32, [I32]),
     "spmlp_head_fill": (I32, [VP, VP, I32, I64, I32, I32, F32, VP]),
     "spmlp_head_prepare": (I32, [VP, VP, VP, I64, I32, I32, F32, VP]),

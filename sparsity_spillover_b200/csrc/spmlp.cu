@@ -392,6 +392,60 @@ int head_fill_impl(void* logits, const int32_t* tiles, int n_tiles, int64_t T, i
   return 0;
 }
 
+// ------------------------------------------------------------ allocation-free MLP forward
+// Workspace of spmlp_mlp_forward_noalloc: h [T, F] (256-byte aligned) followed by
+// the tile bitmap.  A file-scope device array, so the library never calls
+// cudaMalloc for it: the CUDA runtime reserves it on every device where this
+// module is loaded, and it stays reserved until the process exits.
+constexpr size_t kNoAllocScratchBytes = SPMLP_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// symbol is only a stand-in, never a device address; the real address is looked
+// up once per device (cudaGetSymbolAddress, with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(SPMLP_EDEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+int mlp_forward_noalloc_impl(const void* x, const void* w_in, const void* b_in, const void* w_out, const void* b_out,
+                             const void* residual, void* y, int64_t T, int d, int F, int dtype, int gate_op,
+                             float kappa, int64_t seq_len, int mode, uint64_t* stats, cudaStream_t stream) {
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T=%lld must be in [1, 2^31)", (long long)T);
+  if (F < kBitsCols || F % kBitsCols != 0) return fail(SPMLP_ESHAPE, "F=%d must be a positive multiple of 64", F);
+  const size_t h_bytes = ((static_cast<size_t>(T) * static_cast<size_t>(F) * 2) + 255) & ~size_t(255);
+  const size_t bits_bytes = static_cast<size_t>(spmlp_tile_bits_size(T, F)) * 4;
+  if (h_bytes + bits_bytes > kNoAllocScratchBytes)
+    return fail(SPMLP_ESHAPE,
+                "spmlp_mlp_forward_noalloc: T=%lld x F=%d needs %zu bytes of workspace but the static buffer "
+                "holds %zu; split the tokens into smaller calls or use spmlp_mlp_forward",
+                (long long)T, F, h_bytes + bits_bytes, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  void* h = scratch;
+  uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + h_bytes);
+  // up_gate clears the bitmap (cudaMemsetAsync) before its kernel ORs into it,
+  // so nothing the previous call left in the buffer is read.
+  rc = up_gate_impl(x, w_in, b_in, h, bits, nullptr, T, d, F, dtype, gate_op, kappa, seq_len, stream);
+  if (rc) return rc;
+  return down_impl(h, bits, w_out, b_out, residual, y, T, F, d, dtype, mode, stats, stream);
+}
+
 }  // namespace spmlp
 
 using namespace spmlp;
@@ -439,6 +493,13 @@ int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const v
   if (rc) return rc;
   return down_impl(h_workspace, bits_workspace, w_out, b_out, residual, y, T, F, d, dtype, mode, stats,
                    static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_mlp_forward_noalloc(const void* x, const void* w_in, const void* b_in, const void* w_out,
+                              const void* b_out, const void* residual, void* y, int64_t T, int d, int F, int dtype,
+                              int gate_op, float kappa, int64_t seq_len, int mode, uint64_t* stats, void* stream) {
+  return mlp_forward_noalloc_impl(x, w_in, b_in, w_out, b_out, residual, y, T, d, F, dtype, gate_op, kappa, seq_len,
+                                  mode, stats, static_cast<cudaStream_t>(stream));
 }
 
 int spmlp_head_support_words(int d) {
