@@ -12,11 +12,9 @@ from . import gates
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, acc: torch.dtype = torch.float32) -> torch.Tensor:
-    """x w^T + b in ``acc`` precision (nn.Linear's arithmetic without the final cast)."""
-    out = x.to(acc) @ w.to(acc).T
-    if b is not None:
-        out = out + b.to(acc)
-    return out
+    """x w^T + b in ``acc`` precision: nn.Linear's arithmetic (torch.nn.functional.linear,
+    the call inside GPTNeoXMLP's dense layers) on upcast operands, without the final cast."""
+    return torch.nn.functional.linear(x.to(acc), w.to(acc), None if b is None else b.to(acc))
 
 
 def mlp_forward_fp32(x, w_in, b_in, w_out, b_out, gate_op: int, kappa: float, seq_len: int | None = None,
@@ -55,6 +53,25 @@ def down_from_h(h: torch.Tensor, w_out, b_out, residual=None, dtype: torch.dtype
     if residual is not None:
         y = (y.float() + residual.float()).to(dtype)
     return y
+
+
+def joint(h, z, w2, b2, wo, bo, residual, th: float, tz: float, gh: bool, gz: bool):
+    """The reference's joint consumer (parallel residual of GPT-NeoX) in the activation dtype.
+
+    runs/042-2026-09-20-pythia70m-sparse-scale/controls.py:15-27 (NativeJoint) and
+    runs/027-2026-09-06-pythia14m-kernel-sparsity-characterization/test_adapter.py:19-25
+    (joint_reference): gate each branch input with a one-sided threshold, round each
+    branch's linear to the dtype, round the branch sum, then add the residual and round.
+    """
+    dtype = h.dtype
+    if gh:
+        h = h.masked_fill(h < th, 0)
+    if gz:
+        z = z.masked_fill(z < tz, 0)
+    a = linear(h, w2, b2).to(dtype)
+    b = linear(z, wo, bo).to(dtype)
+    s = (a.float() + b.float()).to(dtype)
+    return (s.float() + residual.float()).to(dtype)
 
 
 def max_rel_error(actual: torch.Tensor, reference: torch.Tensor) -> float:
