@@ -33,9 +33,9 @@ METRIC = "gated-MLP fwd tokens/s at 1/2/4/8 B200 and speedup vs dense GEMM by de
 DENSITY = 0.10
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum),
-# summarised in profiles/; None until a capture of the current kernel exists.
-NCU_TRAFFIC_BYTES: dict[str, float | None] = {"up_gate": None, "down_sparse": None}
+# DRAM bytes per launch from one ncu capture of the same layer shape
+# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/gemm_up_down_cfg1.md).
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {"up_gate": 116.4e6, "down_sparse": 187.0e6}
 
 
 def peaks() -> tuple[dict, str]:

@@ -1,0 +1,68 @@
+"""Run a few launches of one kernel on a benchmark config, for profilers (ncu).
+
+    python -m sparsity_spillover_b200.profile_case --case mlp  [--tokens 32768] [--iters 3]
+    python -m sparsity_spillover_b200.profile_case --case tile [--p 0.1]
+    python -m sparsity_spillover_b200.profile_case --case head [--d 128] [--frac 0.1]
+
+* ``mlp``  one cfg1 layer (d=512, F=2048, fp16, one-sided gate at 10% density):
+           up_gate then down_sparse with the residual, ``iters`` times.
+* ``tile`` cfg2: a tile-structured bf16 h (64x64 tiles live with probability p),
+           its bitmap, and the tile-skipping down_sparse (d=512, F=2048).
+* ``head`` cfg4: the N-gated vocabulary head on Zipf-chosen 128-column tiles.
+
+Inputs are seeded synthetic tensors; device memory stays well under 1 GB.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import ops, workloads
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--case", choices=["mlp", "tile", "head"], default="mlp")
+    ap.add_argument("--tokens", type=int, default=32768)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--p", type=float, default=0.1)
+    ap.add_argument("--d", type=int, default=128)
+    ap.add_argument("--frac", type=float, default=0.1)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    with torch.inference_mode():
+        if args.case == "mlp":
+            cfg = workloads.CONFIGS["cfg1"]
+            layer = workloads.make_weights(cfg, dev)[0]
+            x = workloads.make_input(cfg, dev, tokens=args.tokens)
+            z = torch.empty(args.tokens, cfg.F, dtype=cfg.dtype, device=dev)
+            ops.up_gate(x, layer.w_in, layer.b_in, {"operator": "identity"}, z_out=z)
+            gate = {"operator": "one_sided_threshold", "kappa": workloads.quantile_threshold(z, 0.1)}
+            del z
+            h = torch.empty(args.tokens, cfg.F, dtype=cfg.dtype, device=dev)
+            bits = torch.empty(ops.tile_bits_size(args.tokens, cfg.F), dtype=torch.int32, device=dev)
+            y = torch.empty_like(x)
+            for _ in range(args.iters):
+                ops.up_gate(x, layer.w_in, layer.b_in, gate, h=h, bits=bits)
+                ops.down_sparse(h, bits, layer.w_out, layer.b_out, x, y=y)
+        elif args.case == "tile":
+            h, _ = workloads.tile_structured_h(args.tokens, 2048, args.p, seed=3, device=dev)
+            w = (torch.randn(512, 2048, device=dev) * 0.02).bfloat16()
+            bits = ops.tile_bits_from_h(h)
+            y = torch.empty(args.tokens, 512, dtype=torch.bfloat16, device=dev)
+            for _ in range(args.iters):
+                ops.tile_bits_from_h(h, bits)
+                ops.down_sparse(h, bits, w, None, y=y)
+        else:
+            x, w = workloads.head_inputs(args.tokens, args.d, seed=4, device=dev)
+            tiles = torch.from_numpy(workloads.zipf_active_tiles(workloads.VOCAB // 128, args.frac, 5)).to(dev)
+            logits = torch.empty(args.tokens, workloads.VOCAB, dtype=torch.float16, device=dev)
+            for _ in range(args.iters):
+                ops.head_sparse(x, w, active_tiles=tiles, logits=logits)
+        torch.cuda.synchronize(dev)
+    print(f"profile_case {args.case}: ok, device status {ops.device_status(0)}")
+
+
+if __name__ == "__main__":
+    main()
