@@ -51,7 +51,12 @@ extern "C" {
 /* down-projection modes */
 #define SPMLP_DOWN_DENSE 0 /* every K-block multiplied (skipping disabled)          */
 #define SPMLP_DOWN_SKIP 1  /* K-blocks whose 16x64 tiles are all zero for the whole
-                              128-token tile are neither loaded nor multiplied      */
+                              down-projection tile (spmlp_down_tile_tokens(mode)
+                              tokens) are neither loaded nor multiplied; 256-token
+                              tiles on CTA pairs (fastest dense throughput)        */
+#define SPMLP_DOWN_SKIP_FINE 2 /* as SPMLP_DOWN_SKIP with 128-token tiles on single
+                              CTAs: skips more K-blocks when zeros come in token
+                              blocks narrower than 256 (e.g. 64-token tiles)        */
 
 /* error codes (negative returns) */
 #define SPMLP_EINVAL -1   /* bad argument (null pointer, bad enum, non-finite kappa) */
@@ -93,9 +98,13 @@ int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, ui
  *   h [T,F], tile_bits from spmlp_up_gate (ignored for SPMLP_DOWN_DENSE),
  *   w_out [d,F], b_out [d] (nullable), residual [T,d] (nullable) -> y [T,d]
  *   y = round(h w_out^T + b_out), then round(y + residual) when given.
+ *   A K-block (64 features) is skipped for a tile of spmlp_down_tile_tokens(mode)
+ *   tokens when every 16x64 bitmap tile of it in that token range is zero.
  *   stats (nullable, 2 x uint64, accumulated): [0] issued K16 MMA steps,
- *   [1] skipped K16 MMA steps, summed over 128-token x BN tiles.
+ *   [1] skipped K16 MMA steps; one step is one tcgen05.mma over a
+ *   spmlp_down_tile_tokens(mode) x 256 output tile.
  *   Skipping is exact for finite weights (0 * w == 0). */
+int spmlp_down_tile_tokens(int mode);
 int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_out, const void* b_out,
                       const void* residual, void* y, int64_t T, int F, int d, int dtype, int mode,
                       uint64_t* stats, void* stream);

@@ -20,6 +20,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_version": (I32, []),
     "spmlp_last_error": (_c.c_char_p, []),
     "spmlp_tile_bits_words": (I32, [I32]),
+    "spmlp_down_tile_tokens": (I32, [I32]),
     "spmlp_tile_bits_size": (I64, [I64, I32]),
     "spmlp_tile_bits_from_h": (I32, [VP, VP, I64, I32, I32, VP]),
     "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
@@ -37,7 +38,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 # Constants of include/spmlp.h.
 F16, BF16 = 0, 1
 GATE_IDENTITY, GATE_GELU, GATE_ONE_SIDED, GATE_SYMMETRIC, GATE_RELU, GATE_GELU_MASKED, GATE_CORNER = range(7)
-DOWN_DENSE, DOWN_SKIP = 0, 1
+DOWN_DENSE, DOWN_SKIP, DOWN_SKIP_FINE = 0, 1, 2
 HEAD_GATE_NONE, HEAD_GATE_K, HEAD_GATE_N = 0, 1, 2
 
 _lib: ctypes.CDLL | None = None

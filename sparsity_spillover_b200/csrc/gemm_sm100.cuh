@@ -6,7 +6,8 @@
 //               into a STAGES-deep shared-memory ring, so the ring holds the
 //               surviving tiles back to back (compaction through smem).
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128,
-//               N=BN, K=16) into a double-buffered TMEM accumulator.
+//               or M=256 over a CTA pair, N=BN, K=16) into a double-buffered
+//               TMEM accumulator.
 //   warps 2..   epilogue (4 or 8 warps): tcgen05.ld the accumulator (one
 //               token row per thread, software-pipelined), apply the
 //               kind-specific epilogue, stage 32x32 chunks in shared memory
@@ -114,17 +115,18 @@ struct KGran {
   static constexpr int value = (KIND == KIND_HEAD) ? 16 : kBitsCols;
 };
 
-// Live-K mask of one 32-granule chunk for M-tile m_blk.  Warp-collective: lane
-// j tests granule 32*chunk+j across the eight 16-row groups of the tile and
-// __ballot_sync gathers the answer.  Rows past the last row group are absent.
+// Live-K mask of one 32-granule chunk for M-tile m_blk of GROUPS 16-row groups.
+// Warp-collective: lane j tests granule 32*chunk+j across the tile's row groups
+// and __ballot_sync gathers the answer.  Rows past the last row group are absent.
+template <int GROUPS>
 __device__ __forceinline__ uint32_t live_chunk(const uint32_t* bits, int words, int row_groups, int m_blk,
                                                int chunk, int granules, int lane) {
   const int g = chunk * 32 + lane;
   uint32_t live = 0;
   if (g < granules) {
-    const int rg0 = m_blk * (kBM / kBitsRows);
+    const int rg0 = m_blk * GROUPS;
 #pragma unroll
-    for (int r = 0; r < kBM / kBitsRows; ++r) {
+    for (int r = 0; r < GROUPS; ++r) {
       const int rg = rg0 + r;
       if (rg < row_groups) live |= (__ldg(bits + static_cast<size_t>(rg) * words + chunk) >> lane) & 1u;
     }
@@ -141,23 +143,27 @@ __device__ __forceinline__ uint32_t kblocks_of_k16(uint32_t m16) {
   return kb;
 }
 
-template <int KIND, int BN, int STAGES, bool BF16, int EPI = 4, int OUTBUF = 2>
+template <int KIND, int BN, int STAGES, bool BF16, int EPI = 4, int CG = 1>
 struct GemmTraits {
-  static constexpr uint32_t kABytes = kBM * kBK * 2;
-  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr int kTileM = kBM * CG;                   // tokens per (cluster) tile
+  static constexpr uint32_t kABytes = kBM * kBK * 2;         // this CTA's 128 rows of A per stage
+  static constexpr uint32_t kBBytes = (BN / CG) * kBK * 2;   // this CTA's share of B per stage
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator (this CTA's M half)
   static constexpr int kEpiWarps = EPI;          // 4: one warp per TMEM lane quarter; 8: two, splitting columns
   static constexpr int kThreads = 64 + 32 * EPI;
   static constexpr uint32_t kStageOutBytes = 32 * 32 * 2;  // one 32-row x 32-column output chunk
-  static constexpr uint32_t kEpiBytes = EPI * OUTBUF * kStageOutBytes;  // OUTBUF staged chunks per warp
+  static constexpr int kWarpChunks = (BN / 32) / (EPI / 4);  // chunks one epilogue warp handles per tile
+  static constexpr int kFlush = kWarpChunks < 4 ? kWarpChunks : 4;  // chunks per fence + store batch
+  static constexpr uint32_t kEpiBytes = EPI * kWarpChunks * kStageOutBytes;  // a warp's whole tile slab
   static constexpr uint32_t kBiasBytes = EPI * BN * 4;
   static constexpr uint32_t kBarrierBytes = 256;
+  static_assert((2 * STAGES + 5 + EPI) * 8 + 4 <= kBarrierBytes, "barrier region too small");
   static constexpr uint32_t kSmemBytes =
       STAGES * kStageBytes + kEpiBytes + kBiasBytes + kBarrierBytes + 1024;  // +1 KiB for alignment
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair");
   static_assert(EPI == 4 || EPI == 8, "4 or 8 epilogue warps");
-  static_assert(OUTBUF == 2 || OUTBUF == 4 || OUTBUF == 8, "2, 4 or 8 staging buffers per warp");
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB shared-memory limit");
 };
@@ -168,10 +174,10 @@ __device__ __forceinline__ int k_granules(int K) {
   return K / KGran<KIND>::value;
 }
 
-// Enumerate the live K-blocks (64-wide) of an M-tile, calling f(kb, k16_mask)
+// Enumerate the live K-blocks (64-wide) of an M-tile of GROUPS 16-row groups, calling f(kb, k16_mask)
 // for each; k16_mask says which of the block's four K16 steps to issue.
 // Warp-collective (all 32 lanes must call it with the same arguments).
-template <int KIND, class F>
+template <int KIND, int GROUPS, class F>
 __device__ __forceinline__ bool for_each_live_kblock(const GemmParams& p, int m_blk, int lane, F&& f) {
   const int kblocks = p.K / kBK;
   if (!p.skip || p.bits_in == nullptr) {
@@ -183,7 +189,7 @@ __device__ __forceinline__ bool for_each_live_kblock(const GemmParams& p, int m_
   const int granules = k_granules<KIND>(p.K);
   const int chunks = (granules + 31) / 32;
   for (int c = 0; c < chunks; ++c) {
-    const uint32_t mask = live_chunk(p.bits_in, p.bits_words, row_groups, m_blk, c, granules, lane);
+    const uint32_t mask = live_chunk<GROUPS>(p.bits_in, p.bits_words, row_groups, m_blk, c, granules, lane);
     if constexpr (KGran<KIND>::value == kBK) {
       uint32_t pending = mask;
       while (pending) {
@@ -205,11 +211,11 @@ __device__ __forceinline__ bool for_each_live_kblock(const GemmParams& p, int m_
 }
 
 // Count of live K-blocks and of live K16 steps of an M-tile (warp-collective).
-template <int KIND>
+template <int KIND, int GROUPS>
 __device__ __forceinline__ void count_live(const GemmParams& p, int m_blk, int lane, int& blocks, int& steps) {
   blocks = 0;
   steps = 0;
-  for_each_live_kblock<KIND>(p, m_blk, lane, [&](int, uint32_t k16) {
+  for_each_live_kblock<KIND, GROUPS>(p, m_blk, lane, [&](int, uint32_t k16) {
     ++blocks;
     steps += __popc(k16);
     return true;
@@ -319,67 +325,94 @@ struct HeadEpilogue {
 };
 
 // ------------------------------------------------------------------ kernel
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int OUTBUF>
-__global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF>::kThreads, 1)
+// CG = 1: one CTA per 128 x BN tile.  CG = 2: a CTA pair (cluster of 2) per
+// 256 x BN tile: each CTA loads its 128 rows of A and BN/2 rows of B, the
+// leader's single thread issues tcgen05.mma.cta_group::2 (M = 256) over both
+// CTAs' shared memory, and each CTA's TMEM receives its 128-row half.  Stage
+// completion is counted on the leader's barriers; commits multicast to both.
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG>
+__global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                      const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
-  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF>;
+                      const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_r,
+                      const GemmParams p) {
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>;
+  constexpr int kGroups = Tr::kTileM / kBitsRows;  // 16-row bitmap groups per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + STAGES * Tr::kABytes;
-  uint8_t* s_out = smem + STAGES * Tr::kStageBytes;  // [EPI][OUTBUF][32x32] staged output chunks
+  uint8_t* s_out = smem + STAGES * Tr::kStageBytes;  // [EPI][kWarpChunks][32x32] staged output chunks
   float* s_bias = reinterpret_cast<float*>(s_out + Tr::kEpiBytes);  // [EPI][BN]
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_bias) + Tr::kBiasBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
-  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2] (the leader's are the ones used)
   uint64_t* drain = acc_empty + 2;      // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* res_full = drain + 1;       // [EPI]: residual slab loaded (KIND_DOWN)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + EPI);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int total_tiles = p.m_tiles * p.n_tiles;
+  const uint32_t rank = (CG == 1) ? 0u : cluster_ctarank();
+  const bool leader = rank == 0;
+  const int unit = (CG == 1) ? static_cast<int>(blockIdx.x) : static_cast<int>(cluster_id_x());
+  const int units = (CG == 1) ? static_cast<int>(gridDim.x) : static_cast<int>(nclusters_x());
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     tma_prefetch_desc(&tm_c);
+    if (KIND == KIND_DOWN && p.residual != nullptr) tma_prefetch_desc(&tm_r);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], EPI * 32);
+      mbar_init(&acc_empty[i], CG * EPI);  // one arrival per epilogue warp of each CTA
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < EPI; ++i) mbar_init(&res_full[i], 1);
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, Tr::kTmemCols);
+  if (warp == 1) tmem_alloc<CG>(tmem_slot, Tr::kTmemCols);
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 1)
+    __syncthreads();
+  else
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ TMA producer (both CTAs)
     const uint64_t pol_b = l2_policy_evict_last();  // weights: reused by every tile
     int stage = 0;
     uint32_t phase = 0;
     int issued = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+    for (int t = unit; t < total_tiles && ok; t += units) {
       int m_blk, n_col0;
       tile_coords<KIND, BN>(p, t, m_blk, n_col0);
-      ok = for_each_live_kblock<KIND>(p, m_blk, lane, [&](int kb, uint32_t) {
+      const int a_row = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM;
+      const int b_row = n_col0 + static_cast<int>(rank) * (BN / CG);
+      ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int kb, uint32_t) {
         bool good = true;
         if (lane == 0) {
           good = mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutProducer);
           if (good) {
-            mbar_arrive_expect_tx(&full[stage], Tr::kStageBytes);
-            tma_load_2d(s_a + stage * Tr::kABytes, &tm_a, &full[stage], kb * kBK, m_blk * kBM, 0ull);
-            tma_load_2d(s_b + stage * Tr::kBBytes, &tm_b, &full[stage], kb * kBK, n_col0, pol_b);
+            if constexpr (CG == 1) {
+              mbar_arrive_expect_tx(&full[stage], Tr::kStageBytes);
+              tma_load_2d(s_a + stage * Tr::kABytes, &tm_a, &full[stage], kb * kBK, a_row, 0ull);
+              tma_load_2d(s_b + stage * Tr::kBBytes, &tm_b, &full[stage], kb * kBK, b_row, pol_b);
+            } else {
+              // Both CTAs' bytes land on the leader's barrier; only the leader arrives.
+              if (leader) mbar_arrive_expect_tx(&full[stage], CG * Tr::kStageBytes);
+              const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+              tma_load_2d_pair(s_a + stage * Tr::kABytes, &tm_a, bar, kb * kBK, a_row, 0ull);
+              tma_load_2d_pair(s_b + stage * Tr::kBBytes, &tm_b, bar, kb * kBK, b_row, pol_b);
+            }
           }
         }
         good = __shfl_sync(0xffffffffu, good, 0);
@@ -395,136 +428,179 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF
     }
     if (!ok && lane == 0) {
       // Error path: let the copies this warp started land before the CTA exits.
-      const int outstanding = issued < STAGES ? issued : STAGES;
-      int s = stage;
-      uint32_t ph = phase;
-      for (int i = 0; i < outstanding; ++i) {
-        if (--s < 0) {
-          s = STAGES - 1;
-          ph ^= 1u;
+      if constexpr (CG == 1) {
+        const int outstanding = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < outstanding; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1u;
+          }
+          const uint64_t start = global_timer_ns();
+          while (!mbar_try_wait(&full[s], ph)) {
+            if (global_timer_ns() - start > SPMLP_WAIT_NS) {
+              atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
+              break;
+            }
+          }
         }
+      } else {
+        // A pair's copies complete on the leader's barriers, which this CTA
+        // cannot poll; give in-flight bulk copies (microseconds) time to land.
         const uint64_t start = global_timer_ns();
-        while (!mbar_try_wait(&full[s], ph)) {
+        while (global_timer_ns() - start < 200000ull) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader CTA only)
+    constexpr uint32_t idesc = umma_idesc_f16(Tr::kTileM, BN, BF16);
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      unsigned long long issued_steps = 0, skipped_steps = 0;
+      const int k_steps_total = p.K / 16;
+      for (int t = unit; t < total_tiles && ok; t += units) {
+        int m_blk, n_col0;
+        tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+        int live_blocks, live_steps;
+        count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
+        skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
+        issued_steps += static_cast<unsigned long long>(live_steps);
+        if (live_blocks == 0) continue;  // the epilogue writes the zero-accumulator result itself
+        if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        uint32_t accumulate = 0;
+        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int, uint32_t k16) {
+          bool good = true;
+          if (lane == 0) {
+            good = mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma);
+            if (good) {
+              tc_fence_after();
+              const uint64_t a_desc = sw128_kmajor_desc(smem_u32(s_a + stage * Tr::kABytes));
+              const uint64_t b_desc = sw128_kmajor_desc(smem_u32(s_b + stage * Tr::kBBytes));
+#pragma unroll
+              for (int k = 0; k < kBK / 16; ++k) {
+                if ((k16 >> k) & 1u) {
+                  // +32 bytes per K16 step inside the 128-byte swizzled row (>>4 encoded)
+                  umma_f16<CG>(d_tmem, a_desc + static_cast<uint64_t>(2 * k), b_desc + static_cast<uint64_t>(2 * k),
+                               idesc, accumulate);
+                  accumulate = 1;
+                }
+              }
+              umma_commit<CG>(&empty[stage]);
+            }
+          }
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (good && ++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          return good;
+        });
+        if (!ok) break;
+        if (lane == 0) umma_commit<CG>(&acc_full[acc]);
+        __syncwarp();
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (lane == 0) {
+        // Wait for every MMA this thread issued before TMEM is released.
+        umma_commit_local<CG>(drain);
+        const uint64_t start = global_timer_ns();
+        while (!mbar_try_wait(drain, 0)) {
           if (global_timer_ns() - start > SPMLP_WAIT_NS) {
             atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
             break;
           }
         }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = umma_idesc_f16(kBM, BN, BF16);
-    int stage = 0;
-    uint32_t phase = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    bool ok = true;
-    unsigned long long issued_steps = 0, skipped_steps = 0;
-    const int k_steps_total = p.K / 16;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      int m_blk, n_col0;
-      tile_coords<KIND, BN>(p, t, m_blk, n_col0);
-      int live_blocks, live_steps;
-      count_live<KIND>(p, m_blk, lane, live_blocks, live_steps);
-      skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
-      issued_steps += static_cast<unsigned long long>(live_steps);
-      if (live_blocks == 0) continue;  // the epilogue writes the zero-accumulator result itself
-      if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-      uint32_t accumulate = 0;
-      ok = for_each_live_kblock<KIND>(p, m_blk, lane, [&](int, uint32_t k16) {
-        bool good = true;
-        if (lane == 0) {
-          good = mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma);
-          if (good) {
-            tc_fence_after();
-            const uint64_t a_desc = sw128_kmajor_desc(smem_u32(s_a + stage * Tr::kABytes));
-            const uint64_t b_desc = sw128_kmajor_desc(smem_u32(s_b + stage * Tr::kBBytes));
-#pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {
-              if ((k16 >> k) & 1u) {
-                // +32 bytes per K16 step inside the 128-byte swizzled row (>>4 encoded)
-                umma_f16(d_tmem, a_desc + static_cast<uint64_t>(2 * k), b_desc + static_cast<uint64_t>(2 * k),
-                         idesc, accumulate);
-                accumulate = 1;
-              }
-            }
-            umma_commit(&empty[stage]);
-          }
+        if (p.stats != nullptr && KIND != KIND_UP) {
+          atomicAdd(p.stats + 0, issued_steps);
+          atomicAdd(p.stats + 1, skipped_steps);
         }
-        good = __shfl_sync(0xffffffffu, good, 0);
-        if (good && ++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-        return good;
-      });
-      if (!ok) break;
-      if (lane == 0) umma_commit(&acc_full[acc]);
-      __syncwarp();
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
-    }
-    if (lane == 0) {
-      // Wait for every MMA this thread issued before TMEM is released.
-      umma_commit(drain);
-      const uint64_t start = global_timer_ns();
-      while (!mbar_try_wait(drain, 0)) {
-        if (global_timer_ns() - start > SPMLP_WAIT_NS) {
-          atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
-          break;
-        }
-      }
-      if (p.stats != nullptr && KIND != KIND_UP) {
-        atomicAdd(p.stats + 0, issued_steps);
-        atomicAdd(p.stats + 1, skipped_steps);
       }
     }
   } else {
-    // ------------------------------------------------ epilogue warps
+    // ------------------------------------------------ epilogue warps (both CTAs)
     const int ew = warp - 2;               // 0 .. EPI-1
     const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31 (hardware rule: warp id % 4)
-    constexpr int kChunks = BN / 32;
-    constexpr int kMyChunks = kChunks / (EPI / 4);
+    constexpr int kMyChunks = Tr::kWarpChunks;
+    constexpr int kBatches = (kMyChunks + Tr::kFlush - 1) / Tr::kFlush;
     const int ch_begin = (ew / 4) * kMyChunks;  // EPI == 8: the two warps of a quarter split the columns
-    uint8_t* stage_out = s_out + ew * OUTBUF * Tr::kStageOutBytes;
+    uint8_t* stage_out = s_out + ew * kMyChunks * Tr::kStageOutBytes;
     float* bias_s = s_bias + ew * BN;
-    int out_buf = 0;
+    const bool with_res = KIND == KIND_DOWN && p.residual != nullptr;
+    // The accumulator-release barriers live in the leader CTA.
+    uint32_t acc_empty_addr[2];
+    for (int i = 0; i < 2; ++i)
+      acc_empty_addr[i] = (CG == 1) ? smem_u32(&acc_empty[i]) : mapa_shared(smem_u32(&acc_empty[i]), 0);
     int acc = 0;
-    uint32_t acc_phase = 0;
+    uint32_t acc_phase = 0, res_phase = 0;
     const uint32_t k2 = DType<BF16>::pack_rn(p.kappa, p.kappa);  // kappa in both halves (exact: pre-rounded)
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+
+    // Bias of one tile's columns for this warp: lane l holds 8 values (one 16-byte vector).
+    const bool bias_lane = KIND != KIND_HEAD && p.bias != nullptr && lane * 8 < kMyChunks * 32;
+    auto load_bias = [&](int t) -> uint4 {
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+      if (bias_lane && t < total_tiles) {
+        int mb, nc;
+        tile_coords<KIND, BN>(p, t, mb, nc);
+        const int col = nc + ch_begin * 32 + lane * 8;
+        if (col < p.N) raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.bias) + col));
+      }
+      return raw;
+    };
+    uint4 bias_next = load_bias(unit);
+
+    for (int t = unit; t < total_tiles; t += units) {
       int m_blk, n_col0;
       tile_coords<KIND, BN>(p, t, m_blk, n_col0);
       int live_blocks = 1, live_steps = 0;
-      if constexpr (KIND != KIND_UP) count_live<KIND>(p, m_blk, lane, live_blocks, live_steps);
-      const int row0 = m_blk * kBM + quarter * 32;
+      if constexpr (KIND != KIND_UP) count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
+      const int row0 = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const bool has_acc = live_blocks > 0;
 
-      // Bias of this warp's columns -> shared memory (fp32), one 8-value vector per lane.
-      if constexpr (KIND != KIND_HEAD) {
-        __syncwarp();  // every lane is done with the previous tile's bias
-        for (int c = lane * 8; c < kMyChunks * 32; c += 256) {
-          const int col = n_col0 + ch_begin * 32 + c;
-          float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (p.bias != nullptr && col < p.N) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.bias) + col));
-            const uint16_t* rb = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) b[i] = DType<BF16>::to_float(rb[i]);
+      // Residual: TMA it into this warp's output slab while the MMAs run.  The
+      // previous tile's stores must first have read the slab.
+      if (with_res) {
+        if (lane == 0) {
+          bulk_wait_group_read<0>();
+          if (row0 < p.M) {
+            int n_in = 0;
+            for (int i = 0; i < kMyChunks; ++i) n_in += (n_col0 + (ch_begin + i) * 32 < p.N) ? 1 : 0;
+            mbar_arrive_expect_tx(&res_full[ew], n_in * Tr::kStageOutBytes);
+            for (int i = 0; i < kMyChunks; ++i) {
+              const int c0 = n_col0 + (ch_begin + i) * 32;
+              if (c0 < p.N) tma_load_2d(stage_out + i * Tr::kStageOutBytes, &tm_r, &res_full[ew], c0, row0, 0ull);
+            }
           }
-          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + c)[0] = make_float4(b[0], b[1], b[2], b[3]);
-          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + c)[1] = make_float4(b[4], b[5], b[6], b[7]);
         }
         __syncwarp();
+      }
+
+      // Bias of this tile -> shared memory (fp32); the next tile's is fetched now.
+      if constexpr (KIND != KIND_HEAD) {
+        __syncwarp();  // every lane is done with the previous tile's bias
+        if (lane * 8 < kMyChunks * 32) {
+          const uint16_t* rb = reinterpret_cast<const uint16_t*>(&bias_next);
+          float b[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) b[i] = DType<BF16>::to_float(rb[i]);
+          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + lane * 8)[0] = make_float4(b[0], b[1], b[2], b[3]);
+          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + lane * 8)[1] = make_float4(b[4], b[5], b[6], b[7]);
+        }
+        __syncwarp();
+        bias_next = load_bias(t + units);
       }
 
       if (has_acc) {
@@ -533,89 +609,101 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF
         if (!good) break;
         tc_fence_after();
       }
+      if (with_res && row0 < p.M) {
+        const bool good = __all_sync(0xffffffffu, mbar_wait(&res_full[ew], res_phase, p.status, kDevTimeoutEpilogue));
+        res_phase ^= 1u;
+        if (!good) break;
+      }
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
 
-      // Residual prefetch (KIND_DOWN): 64 contiguous bytes of this row per chunk.
-      auto load_res = [&](int ch, uint4 (&r)[4]) {
-        if (KIND == KIND_DOWN && p.residual != nullptr && row_ok && n_col0 + ch * 32 < p.N) {
-          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.residual) +
-                                                            static_cast<size_t>(row) * p.N + n_col0 + ch * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) r[i] = __ldg(src + i);
+      // Release the accumulator (once per warp) when its last TMEM load completed.
+      auto release_acc = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1)
+            mbar_arrive(&acc_empty[acc]);
+          else
+            mbar_arrive_cluster(acc_empty_addr[acc]);
         }
       };
 
       uint32_t nz_bits = 0;  // KIND_UP: bit (2*group + half) per 64-column group of the tile
-      auto process = [&](int ch, const uint32_t (&v)[32], const uint4 (&r)[4]) {
+      const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this lane's row in a 32x32 chunk
+      auto process = [&](int ch, const uint32_t (&v)[32]) {
         const int col0 = n_col0 + ch * 32;
-        if (col0 >= p.N) return;  // N is a multiple of 64: whole chunk out of range
-        uint32_t packed[16];
-        bool nz = false;
-        if constexpr (KIND == KIND_UP)
-          nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + ch * 32, k2, packed);
-        else if constexpr (KIND == KIND_DOWN)
-          DownEpilogue<BF16>::apply(p, v, bias_s + ch * 32, r, packed);
-        else
-          HeadEpilogue<BF16>::apply(v, packed);
-        if constexpr (KIND == KIND_UP) {
-          const uint32_t ball = __ballot_sync(0xffffffffu, nz);
-          const int grp = ch >> 1;
-          if (ball & 0x0000ffffu) nz_bits |= 1u << (2 * grp);
-          if (ball & 0xffff0000u) nz_bits |= 1u << (2 * grp + 1);
+        const int slot = ch - ch_begin;
+        uint8_t* buf = stage_out + slot * Tr::kStageOutBytes;
+        if (!with_res && slot % Tr::kFlush == 0) {
+          // The store batch that last used these slots has read them.
+          if (lane == 0) bulk_wait_group_read<kBatches - 1>();
+          __syncwarp();
         }
-        // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) and hand it to TMA.
-        uint8_t* buf = stage_out + out_buf * Tr::kStageOutBytes;
-        if (lane == 0) bulk_wait_group_read<OUTBUF - 1>();  // the store that last used `buf` has read it
-        __syncwarp();
-        const int sw = (lane >> 1) & 3;
+        if (col0 < p.N) {  // N is a multiple of 64: a chunk is wholly in or out of range
+          uint32_t packed[16];
+          bool nz = false;
+          if constexpr (KIND == KIND_UP) {
+            nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + ch * 32, k2, packed);
+          } else if constexpr (KIND == KIND_DOWN) {
+            uint4 r[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
+                          make_uint4(0u, 0u, 0u, 0u)};
+            if (with_res) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
-              make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (row0 < p.M) tma_store_2d(&tm_c, buf, col0, row0);
-          bulk_commit_group();
+              for (int c = 0; c < 4; ++c) r[c] = *reinterpret_cast<const uint4*>(buf + lane * 64 + ((c ^ sw) << 4));
+            }
+            DownEpilogue<BF16>::apply(p, v, bias_s + ch * 32, r, packed);
+          } else {
+            HeadEpilogue<BF16>::apply(v, packed);
+          }
+          if constexpr (KIND == KIND_UP) {
+            const uint32_t ball = __ballot_sync(0xffffffffu, nz);
+            const int grp = ch >> 1;
+            if (ball & 0x0000ffffu) nz_bits |= 1u << (2 * grp);
+            if (ball & 0xffff0000u) nz_bits |= 1u << (2 * grp + 1);
+          }
+          // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) in this warp's tile slab.
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
+                make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
         }
-        out_buf = (out_buf + 1) % OUTBUF;
+        // Every kFlush chunks: one fence and one batch of TMA stores for the staged chunks.
+        if ((slot + 1) % Tr::kFlush == 0 || slot + 1 == kMyChunks) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < p.M) {
+            for (int i = slot - slot % Tr::kFlush; i <= slot; ++i) {
+              const int c0 = n_col0 + (ch_begin + i) * 32;
+              if (c0 < p.N) tma_store_2d(&tm_c, stage_out + i * Tr::kStageOutBytes, c0, row0);
+            }
+          }
+          if (lane == 0) bulk_commit_group();
+        }
       };
 
       uint32_t va[32], vb[32];
-      uint4 ra[4], rb[4];
 #pragma unroll
       for (int j = 0; j < 32; ++j) va[j] = vb[j] = 0u;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ra[i] = rb[i] = make_uint4(0u, 0u, 0u, 0u);
       const int ch_end = ch_begin + kMyChunks;
       if (has_acc) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch_begin * 32), va);
-      load_res(ch_begin, ra);
 #pragma unroll 1
       for (int ch = ch_begin; ch < ch_end; ch += 2) {
-        // even chunk: va / ra
+        // even chunk: va
         if (has_acc) {
           tmem_wait_ld(va);
           if (ch + 1 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 1) * 32), vb);
-          if (ch + 1 >= ch_end) {  // accumulator fully read: release it to the MMA warp
-            tc_fence_before();
-            mbar_arrive(&acc_empty[acc]);
-          }
+          if (ch + 1 >= ch_end) release_acc();
         }
-        if (ch + 1 < ch_end) load_res(ch + 1, rb);
-        process(ch, va, ra);
+        process(ch, va);
         if (ch + 1 < ch_end) {
-          // odd chunk: vb / rb
+          // odd chunk: vb
           if (has_acc) {
             tmem_wait_ld(vb);
             if (ch + 2 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 2) * 32), va);
-            if (ch + 2 >= ch_end) {
-              tc_fence_before();
-              mbar_arrive(&acc_empty[acc]);
-            }
+            if (ch + 2 >= ch_end) release_acc();
           }
-          if (ch + 2 < ch_end) load_res(ch + 2, ra);
-          process(ch + 1, vb, rb);
+          process(ch + 1, vb);
         }
       }
       if constexpr (KIND == KIND_UP) {
@@ -628,7 +716,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF
             uint32_t w = 0;
             for (int grp = 0; grp < BN / kBitsCols; ++grp)
               if ((nz_bits >> (2 * grp + half)) & 1u) w |= 1u << (shift + grp);
-            const int rg = m_blk * (kBM / kBitsRows) + quarter * 2 + half;
+            const int rg = (row0 >> 4) + half;
             if (w != 0) atomicOr(p.bits_out + static_cast<size_t>(rg) * p.bits_words + word, w);
           }
         }
@@ -643,10 +731,13 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 1)
+    __syncthreads();
+  else
+    cluster_sync();  // the pair's MMAs and cross-CTA arrivals are finished
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Tr::kTmemCols);
+    tmem_dealloc<CG>(tmem_base, Tr::kTmemCols);
   }
 }
 

@@ -44,7 +44,11 @@ constexpr int kMaxDevices = 64;
 
 // Tile configuration of the up-projection: pipeline stages, epilogue warps,
 // staged output chunks per epilogue warp (tuned on B200 for d=512, F=2048).
-constexpr int kUpStages = 3, kUpEpiWarps = 4, kUpOutBufs = 4;
+constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2;
+// Down-projection, dense and coarse-skip modes: 256-token tiles on CTA pairs.
+constexpr int kDownStages = 4, kDownEpiWarps = 8, kDownCG = 2;
+// Down-projection, fine-skip mode: 128-token tiles on single CTAs.
+constexpr int kDownFineStages = 3, kDownFineEpiWarps = 4;
 
 struct DeviceInfo {
   int sm_count = 0;
@@ -130,19 +134,51 @@ int make_out_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- launch
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int OUTBUF>
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
-                cudaStream_t stream, DeviceInfo* dev) {
-  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, OUTBUF>;
-  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, OUTBUF>;
+                cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr) {
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>;
+  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG>;
   // Setting the attribute is per function; cheap and idempotent.
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  p.m_tiles = (p.M + Tr::kTileM - 1) / Tr::kTileM;
   const int tiles = p.m_tiles * p.n_tiles;
   if (tiles == 0) return 0;
-  const int grid = tiles < dev->sm_count ? tiles : dev->sm_count;
   p.status = dev->status;
-  kernel<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(ta, tb, tc, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(Tr::kThreads);
+  cfg.dynamicSmemBytes = Tr::kSmemBytes;
+  cfg.stream = stream;
+  int units = dev->sm_count;  // persistent: one CTA (or CTA pair) per SM (pair)
+  if constexpr (CG > 1) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(cluster size)");
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Clusters that can be resident at once, queried once per device for this kernel.
+    static int max_clusters[kMaxDevices] = {};
+    int dev_id = 0;
+    cudaGetDevice(&dev_id);
+    if (max_clusters[dev_id] == 0) {
+      cfg.gridDim = dim3(dev->sm_count);
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+      if (e != cudaSuccess || n <= 0) return cuda_fail(e == cudaSuccess ? cudaErrorInvalidConfiguration : e,
+                                                       "cudaOccupancyMaxActiveClusters");
+      max_clusters[dev_id] = n;
+    }
+    units = max_clusters[dev_id];
+  }
+  if (tiles < units) units = tiles;
+  cfg.gridDim = dim3(units * CG);
+  e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr != nullptr ? *tr : tc, p);
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return 0;
@@ -152,11 +188,11 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 template <int BN>
 int launch_up(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int gate_op,
               bool bf16, cudaStream_t stream, DeviceInfo* dev) {
-  constexpr int S = kUpStages, E = kUpEpiWarps, B = kUpOutBufs;
-#define SPMLP_UP_CASE(G)                                                                   \
-  case G:                                                                                  \
-    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, B>(ta, tb, tc, p, stream, dev)   \
-                : launch_gemm<KIND_UP, G, BN, S, false, E, B>(ta, tb, tc, p, stream, dev);
+  constexpr int S = kUpStages, E = kUpEpiWarps, C = kUpCG;
+#define SPMLP_UP_CASE(G)                                                                     \
+  case G:                                                                                    \
+    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C>(ta, tb, tc, p, stream, dev)     \
+                : launch_gemm<KIND_UP, G, BN, S, false, E, C>(ta, tb, tc, p, stream, dev);
   switch (gate_op) {
     SPMLP_UP_CASE(GATE_IDENTITY)
     SPMLP_UP_CASE(GATE_GELU)
@@ -215,7 +251,7 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   constexpr int BN = 256;
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
-  if ((rc = make_kmajor_map(&tb, w_in, F, d, BN, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb, w_in, F, d, BN / kUpCG, bf16))) return rc;
   CUtensorMap tc;
   if ((rc = make_out_map(&tc, h, T, F, bf16))) return rc;
   const int words = spmlp_tile_bits_words(F);
@@ -226,7 +262,6 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   p.M = static_cast<int>(T);
   p.N = F;
   p.K = d;
-  p.m_tiles = static_cast<int>((T + kBM - 1) / kBM);
   p.n_tiles = (F + BN - 1) / BN;
   p.bias = b_in;
   p.out = h;
@@ -243,8 +278,9 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
               int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, cudaStream_t stream) {
   int rc;
   if (!h || !w_out || !y) return fail(SPMLP_EINVAL, "h, w_out and y must be non-null");
-  if (mode != SPMLP_DOWN_DENSE && mode != SPMLP_DOWN_SKIP) return fail(SPMLP_EINVAL, "unknown down mode %d", mode);
-  if (mode == SPMLP_DOWN_SKIP && !bits) return fail(SPMLP_EINVAL, "SPMLP_DOWN_SKIP needs tile_bits");
+  if (mode != SPMLP_DOWN_DENSE && mode != SPMLP_DOWN_SKIP && mode != SPMLP_DOWN_SKIP_FINE)
+    return fail(SPMLP_EINVAL, "unknown down mode %d", mode);
+  if (mode != SPMLP_DOWN_DENSE && !bits) return fail(SPMLP_EINVAL, "the skipping down modes need tile_bits");
   if ((rc = check_dtype(dtype))) return rc;
   if ((rc = check_mk(T, F, d, "F", "d"))) return rc;
   if (!aligned16(h) || !aligned16(w_out) || !aligned16(y) || (b_out && !aligned16(b_out)) ||
@@ -257,24 +293,32 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   constexpr int BN = 256;
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
-  if ((rc = make_kmajor_map(&tb, w_out, d, F, BN, bf16))) return rc;
-  CUtensorMap tc;
+  const int cg = mode == SPMLP_DOWN_SKIP_FINE ? 1 : kDownCG;
+  if ((rc = make_kmajor_map(&tb, w_out, d, F, BN / cg, bf16))) return rc;
+  CUtensorMap tc, tr;
   if ((rc = make_out_map(&tc, y, T, d, bf16))) return rc;
+  if (residual != nullptr && (rc = make_out_map(&tr, residual, T, d, bf16))) return rc;
   GemmParams p{};
   p.M = static_cast<int>(T);
   p.N = d;
   p.K = F;
-  p.m_tiles = static_cast<int>((T + kBM - 1) / kBM);
   p.n_tiles = (d + BN - 1) / BN;
   p.bias = b_out;
   p.out = y;
   p.residual = residual;
   p.bits_in = bits;
   p.bits_words = spmlp_tile_bits_words(F);
-  p.skip = mode == SPMLP_DOWN_SKIP ? 1 : 0;
+  p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, 4, true, 4, 2>(ta, tb, tc, p, stream, dev);
-  return launch_gemm<KIND_DOWN, 0, BN, 4, false, 4, 2>(ta, tb, tc, p, stream, dev);
+  constexpr int S = kDownStages, E = kDownEpiWarps, C = kDownCG;
+  constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps;
+  const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
+  if (mode == SPMLP_DOWN_SKIP_FINE) {
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, SF, true, EF, 1>(ta, tb, tc, p, stream, dev, trp);
+    return launch_gemm<KIND_DOWN, 0, BN, SF, false, EF, 1>(ta, tb, tc, p, stream, dev, trp);
+  }
+  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C>(ta, tb, tc, p, stream, dev, trp);
+  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C>(ta, tb, tc, p, stream, dev, trp);
 }
 
 
@@ -351,7 +395,6 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   p.M = static_cast<int>(T);
   p.N = V;
   p.K = d;
-  p.m_tiles = static_cast<int>((T + kBM - 1) / kBM);
   p.n_tiles = gate_axis == SPMLP_HEAD_GATE_N ? n_active : V / BN;
   p.out = logits;
   p.col_tiles = gate_axis == SPMLP_HEAD_GATE_N ? active : nullptr;
@@ -359,8 +402,8 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   p.bits_words = spmlp_head_support_words(d);
   p.skip = gate_axis == SPMLP_HEAD_GATE_K ? 1 : 0;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  if (bf16) return launch_gemm<KIND_HEAD, 0, BN, 6, true, 4, 2>(ta, tb, tc, p, stream, dev);
-  return launch_gemm<KIND_HEAD, 0, BN, 6, false, 4, 2>(ta, tb, tc, p, stream, dev);
+  if (bf16) return launch_gemm<KIND_HEAD, 0, BN, 4, true, 4, 1>(ta, tb, tc, p, stream, dev);
+  return launch_gemm<KIND_HEAD, 0, BN, 4, false, 4, 1>(ta, tb, tc, p, stream, dev);
 }
 
 int head_fill_impl(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype, float value,
@@ -453,6 +496,8 @@ using namespace spmlp;
 extern "C" {
 
 int spmlp_version(void) { return 100; }
+
+int spmlp_down_tile_tokens(int mode) { return mode == SPMLP_DOWN_SKIP_FINE ? kBM : kBM * kDownCG; }
 
 const char* spmlp_last_error(void) { return g_last_error.c_str(); }
 

@@ -51,6 +51,22 @@ def tile_bits_size(tokens: int, features: int) -> int:
     return int(_lib.load().spmlp_tile_bits_size(tokens, features))
 
 
+def _down_mode(skip: bool | str) -> int:
+    if skip is False:
+        return _lib.DOWN_DENSE
+    if skip is True or skip == "coarse":
+        return _lib.DOWN_SKIP
+    if skip == "fine":
+        return _lib.DOWN_SKIP_FINE
+    raise ValueError("skip must be True/'coarse', 'fine' or False")
+
+
+def down_tile_tokens(skip: bool | str = True) -> int:
+    """Tokens per down-projection tile for a skip setting: the granularity of
+    K-block skipping and of the issued/skipped counters."""
+    return int(_lib.load().spmlp_down_tile_tokens(_down_mode(skip)))
+
+
 def tile_bits_words(features: int) -> int:
     return int(_lib.load().spmlp_tile_bits_words(features))
 
@@ -101,11 +117,13 @@ def up_gate(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, gate
 
 
 def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor, b_out: torch.Tensor | None,
-                residual: torch.Tensor | None = None, *, skip: bool = True, y: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None, *, skip: bool | str = True, y: torch.Tensor | None = None,
                 stats: torch.Tensor | None = None) -> torch.Tensor:
     """y = round(h w_out^T + b_out) [then round(y + residual)], skipping dead 16x64 K-tiles.
 
     h [T,F], w_out [d,F], b_out [d] or None, residual [T,d] or None.
+    skip: True / "coarse" (256-token tiles on CTA pairs), "fine" (128-token tiles,
+    finer skipping for token-blocked zeros) or False (dense).
     stats: optional int64[2] device tensor accumulating issued / skipped K16 steps.
     """
     device, dtype, code = _device_dtype(h)
@@ -117,9 +135,10 @@ def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor,
         _check("b_out", b_out, dtype, device, (d,))
     if residual is not None:
         _check("residual", residual, dtype, device, (t, d))
-    if skip:
+    mode = _down_mode(skip)
+    if mode != _lib.DOWN_DENSE:
         if bits is None:
-            raise ValueError("skip=True needs the tile bitmap")
+            raise ValueError("skipping needs the tile bitmap")
         _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
     if y is None:
         y = torch.empty((t, d), device=device, dtype=dtype)
@@ -127,14 +146,13 @@ def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor,
     if stats is not None:
         _check("stats", stats, torch.int64, device, (2,))
     with torch.cuda.device(device):
-        _lib.call("spmlp_down_sparse", _ptr(h), _ptr(bits) if skip else None, _ptr(w_out), _ptr(b_out),
-                  _ptr(residual), _ptr(y), t, f, d, code, _lib.DOWN_SKIP if skip else _lib.DOWN_DENSE,
-                  _ptr(stats), _stream(device))
+        _lib.call("spmlp_down_sparse", _ptr(h), _ptr(bits) if mode != _lib.DOWN_DENSE else None, _ptr(w_out),
+                  _ptr(b_out), _ptr(residual), _ptr(y), t, f, d, code, mode, _ptr(stats), _stream(device))
     return y
 
 
 def mlp_forward(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, w_out: torch.Tensor,
-                b_out: torch.Tensor | None, gate=None, *, residual: torch.Tensor | None = None, skip: bool = True,
+                b_out: torch.Tensor | None, gate=None, *, residual: torch.Tensor | None = None, skip: bool | str = True,
                 h: torch.Tensor | None = None, bits: torch.Tensor | None = None, y: torch.Tensor | None = None,
                 stats: torch.Tensor | None = None, seq_len: int | None = None) -> torch.Tensor:
     """GPTNeoXMLP.forward with a fused gate: both kernels, h/bits as reusable workspace."""

@@ -107,7 +107,8 @@ def test_up_gate_matches_reference_gate_on_kernel_z(dtype, op, shape):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("density", [1.0, 0.25, 0.1, 0.02])
-def test_down_sparse_matches_fp32_oracle(dtype, density):
+@pytest.mark.parametrize("skip", [True, "fine"])
+def test_down_sparse_matches_fp32_oracle(dtype, density, skip):
     from sparsity_spillover_b200 import ops
 
     t, d, f = 1536, 512, 2048
@@ -117,7 +118,7 @@ def test_down_sparse_matches_fp32_oracle(dtype, density):
     xd, wd, bd, wod, bod = _cuda(x, w_in, b_in, w_out, b_out)
     h, bits = ops.up_gate(xd, wd, bd, gate)
     stats = torch.zeros(2, dtype=torch.int64, device=DEV)
-    y_skip = ops.down_sparse(h, bits, wod, bod, skip=True, stats=stats)
+    y_skip = ops.down_sparse(h, bits, wod, bod, skip=skip, stats=stats)
     y_dense = ops.down_sparse(h, None, wod, bod, skip=False)
     torch.cuda.synchronize()
     h_c = h.cpu()
@@ -125,7 +126,7 @@ def test_down_sparse_matches_fp32_oracle(dtype, density):
     assert omlp.max_rel_error(y_skip.cpu(), y_ref) <= TOL[dtype]
     assert torch.equal(y_skip, y_dense)
     mask = obit.tile_mask(h_c)
-    issued, skipped = obit.skip_counts(mask, f, n_tiles=(d + 255) // 256)
+    issued, skipped = obit.skip_counts(mask, f, n_tiles=(d + 255) // 256, m_tile=ops.down_tile_tokens(skip))
     assert stats.cpu().tolist() == [issued, skipped]
 
 
@@ -172,7 +173,8 @@ def test_mlp_end_to_end_against_dtype_oracle(dtype):
     assert report["pass"], report
 
 
-def test_tile_structured_h_skips_dead_tiles():
+@pytest.mark.parametrize("skip", [True, "fine"])
+def test_tile_structured_h_skips_dead_tiles(skip):
     """cfg2-style input: 64x64 tiles live with p=0.2; skip == dense, counters match the oracle."""
     from sparsity_spillover_b200 import ops, workloads
 
@@ -183,14 +185,14 @@ def test_tile_structured_h_skips_dead_tiles():
     b_out = (torch.randn(d, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
     bits = ops.tile_bits_from_h(h)
     stats = torch.zeros(2, dtype=torch.int64, device=DEV)
-    y = ops.down_sparse(h, bits, w_out, b_out, stats=stats)
+    y = ops.down_sparse(h, bits, w_out, b_out, skip=skip, stats=stats)
     y_dense = ops.down_sparse(h, None, w_out, b_out, skip=False)
     torch.cuda.synchronize()
     h_c = h.cpu()
     np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), obit.tile_bits(h_c))
     assert torch.equal(y, y_dense)
     assert omlp.max_rel_error(y.cpu(), omlp.down_from_h(h_c, w_out.cpu(), b_out.cpu())) <= TOL[torch.bfloat16]
-    issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=1)
+    issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=1, m_tile=ops.down_tile_tokens(skip))
     assert stats.cpu().tolist() == [issued, skipped]
     assert skipped > 0
 

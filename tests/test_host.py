@@ -41,6 +41,7 @@ def test_pure_host_entry_points(lib):
     assert lib.spmlp_tile_bits_size(1000, 320) == 63
     assert lib.spmlp_head_support_words(128) == 1
     assert lib.spmlp_head_support_words(1024) == 2
+    assert lib.spmlp_down_tile_tokens(1) == 256 and lib.spmlp_down_tile_tokens(2) == 128
     assert lib.spmlp_last_error() is not None
 
 
