@@ -149,12 +149,12 @@ def barrier(world: int, device=None):
 class Stack:
     """Weights, calibrated gates and activation buffers of the 6-layer workload on one GPU."""
 
-    def __init__(self, device, rank: int, density: float):
+    def __init__(self, device, rank: int, density: float, cfg_name: str = "cfg1"):
         import torch
 
         from sparsity_spillover_b200 import ops, workloads
 
-        self.cfg = cfg = workloads.CONFIGS["cfg1"]
+        self.cfg = cfg = workloads.CONFIGS[cfg_name]
         self.device = device
         self.layers = workloads.make_weights(cfg, device)
         self.x0 = workloads.make_input(cfg, device, token_offset=rank)
@@ -213,9 +213,128 @@ def dense_reference_step(stack: Stack):
     return x
 
 
+def graph_of(fn, device):
+    """Capture fn() once as a CUDA graph on a side stream."""
+    import torch
+
+    fn()
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    return g
+
+
+def density_sweep(device, densities=(1.0, 0.5, 0.25, 0.1, 0.05), steps=5) -> list[dict]:
+    """cfg1 at each density: our 6-layer step vs the stock PyTorch forward (both graph-replayed)."""
+    import torch
+
+    rows = []
+    for rho in densities:
+        st = Stack(device, 0, rho)
+        g_ours = graph_of(st.step, device)
+        g_ref = graph_of(lambda: dense_reference_step(st), device)
+        t_ours = time_device(g_ours.replay, steps, device)
+        t_ref = time_device(g_ref.replay, steps, device)
+        issued, skipped = st.stats.cpu().tolist()
+        rows.append({"density_target": rho, "density_measured": round(st.density, 4),
+                     "tokens_per_s": st.cfg.tokens / t_ours, "dense_pytorch_tokens_per_s": st.cfg.tokens / t_ref,
+                     "speedup_vs_dense_pytorch": t_ref / t_ours, "skipped_k16_fraction": skipped / max(1, issued + skipped)})
+        del g_ours, g_ref, st
+        torch.cuda.empty_cache()
+    base = rows[0]["tokens_per_s"]
+    for r in rows:
+        r["speedup_vs_ours_at_100pct"] = r["tokens_per_s"] / base
+    return rows
+
+
+def tile_structured(device, steps=10) -> list[dict]:
+    """cfg2: tile-structured h (64x64 tiles live with probability p), bf16, T=65536: the
+    skipping down-projection against its dense mode and cuBLAS."""
+    import torch
+
+    from sparsity_spillover_b200 import ops, workloads
+
+    rows = []
+    for d, f in ((256, 1024), (512, 2048)):
+        g = torch.Generator(device=device).manual_seed(20 + d)
+        w = (torch.randn(d, f, generator=g, device=device) * 0.02).bfloat16()
+        for p in (0.5, 0.2, 0.1):
+            h, frac = workloads.tile_structured_h(65536, f, p, seed=int(p * 100) + d, device=device)
+            bits = ops.tile_bits_from_h(h)
+            y = torch.empty(65536, d, dtype=torch.bfloat16, device=device)
+            stats = {}
+            times = {}
+            for mode in ("fine", True, False):
+                st = torch.zeros(2, dtype=torch.int64, device=device)
+                ops.down_sparse(h, bits, w, None, skip=mode, y=y, stats=st)
+                stats[str(mode)] = st.cpu().tolist()
+                times[str(mode)] = time_device(lambda: ops.down_sparse(h, bits, w, None, skip=mode, y=y), steps, device)
+            t_cublas = time_device(lambda: torch.nn.functional.linear(h, w), steps, device)
+            t_bits = time_device(lambda: ops.tile_bits_from_h(h, bits), steps, device)
+            fi = stats["fine"]
+            rows.append({"d": d, "F": f, "p": p, "live_tile_fraction": round(frac, 4),
+                         "down_fine_us": times["fine"] * 1e6, "down_coarse_us": times["True"] * 1e6,
+                         "down_dense_us": times["False"] * 1e6, "cublas_us": t_cublas * 1e6, "bitmap_us": t_bits * 1e6,
+                         "skipped_k16_fraction_fine": fi[1] / max(1, fi[0] + fi[1]),
+                         "speedup_fine_vs_dense": times["False"] / times["fine"],
+                         "speedup_fine_vs_cublas": t_cublas / times["fine"], "ideal_speedup": 1.0 / max(frac, 1e-9)})
+            del h, bits, y
+        torch.cuda.empty_cache()
+    return rows
+
+
+def cfg3_410m(device, steps=3) -> dict:
+    """cfg3: Pythia-410M shape, 24 layers, d=1024 F=4096, T=32768 per GPU, fp16, 10% density."""
+    import torch
+
+    st = Stack(device, 0, DENSITY, cfg_name="cfg3")
+    g_ours = graph_of(st.step, device)
+    g_ref = graph_of(lambda: dense_reference_step(st), device)
+    t_ours = time_device(g_ours.replay, steps, device)
+    t_ref = time_device(g_ref.replay, steps, device)
+    cfg = st.cfg
+    flop = cfg.layers * 2 * (2.0 * cfg.tokens * cfg.d * cfg.F)
+    out = {"tokens_per_s": cfg.tokens / t_ours, "ms_per_step": t_ours * 1e3, "dense_pytorch_tokens_per_s": cfg.tokens / t_ref,
+           "speedup_vs_dense_pytorch": t_ref / t_ours, "executed_tflops": flop / t_ours / 1e12,
+           "density_measured": round(st.density, 4)}
+    del g_ours, g_ref, st
+    torch.cuda.empty_cache()
+    return out
+
+
+def head_bench(device, steps=5) -> list[dict]:
+    """cfg4: embed_out [32768, d] x [d, 50304] fp16 with Zipf(1.1)-chosen active 128-column tiles."""
+    import torch
+
+    from sparsity_spillover_b200 import ops, workloads
+
+    rows = []
+    t_tokens = 32768
+    for d in (128, 512):
+        x, w = workloads.head_inputs(t_tokens, d, seed=40 + d, device=device)
+        logits = torch.empty(t_tokens, workloads.VOCAB, dtype=torch.float16, device=device)
+        t_dense = time_device(lambda: ops.head_sparse(x, w, logits=logits), steps, device)
+        t_cublas = time_device(lambda: torch.nn.functional.linear(x, w), steps, device)
+        for frac in (0.05, 0.1, 0.25):
+            tiles = torch.from_numpy(workloads.zipf_active_tiles(workloads.VOCAB // 128, frac, seed=7)).to(device)
+            t_n = time_device(lambda: ops.head_sparse(x, w, active_tiles=tiles, logits=logits), steps, device)
+            rows.append({"d": d, "active_fraction": frac, "n_gated_us": t_n * 1e6, "dense_us": t_dense * 1e6,
+                         "cublas_us": t_cublas * 1e6, "speedup_vs_cublas": t_cublas / t_n,
+                         "logit_write_gbs": t_tokens * tiles.numel() * 128 * 2 / t_n / 1e9})
+        del x, w, logits
+        torch.cuda.empty_cache()
+    return rows
+
+
 def time_device(fn, steps: int, device) -> float:
     import torch
 
+    fn()  # warm-up (first-call library heuristics, lazy set-up)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(device)
     start.record()
@@ -407,6 +526,14 @@ def run_ours(args):
         "clocks": clocks,
         "device_status": status,
     }
+    if world == 1 and not args.no_extras:
+        import torch
+
+        with torch.inference_mode():
+            line["density_sweep"] = density_sweep(device)
+            line["tile_structured_cfg2"] = tile_structured(device)
+            line["pythia410m_cfg3"] = cfg3_410m(device)
+            line["vocab_head_cfg4"] = head_bench(device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
     if world > 1:
@@ -455,6 +582,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-config sweeps (density, cfg2, cfg3, cfg4)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
