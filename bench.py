@@ -331,6 +331,49 @@ def head_bench(device, steps=5) -> list[dict]:
     return rows
 
 
+def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int = 3) -> dict:
+    """410M shape, `layers` layers: d_ff split over the ranks (reduce-scatter + all-gather per
+    layer over NCCL) against token sharding of the same per-rank token count (no collective)."""
+    import torch
+    import torch.distributed as dist
+
+    from sparsity_spillover_b200 import dist as sdist
+    from sparsity_spillover_b200 import ops, workloads
+
+    cfg = workloads.CONFIGS["cfg3"]
+    full = workloads.make_weights(cfg, device)[:layers]
+    gate = {"operator": "one_sided_threshold", "kappa": 0.58}
+    t_rank = cfg.tokens
+    x_all = workloads.make_input(cfg, device, tokens=t_rank * world)  # the same token block on every rank
+    split = [sdist.DffSplitMLP.from_full(L.w_in, L.b_in, L.w_out, L.b_out, gate, world, rank) for L in full]
+
+    def run_split():
+        return sdist.dff_split_forward(split, x_all)
+
+    x_mine = x_all[rank * t_rank:(rank + 1) * t_rank].contiguous()
+    h = torch.empty(t_rank, cfg.F, dtype=cfg.dtype, device=device)
+    bits = torch.empty(ops.tile_bits_size(t_rank, cfg.F), dtype=torch.int32, device=device)
+    bufs = [torch.empty_like(x_mine) for _ in range(2)]
+
+    def run_tokens():
+        cur = x_mine
+        for i, L in enumerate(full):
+            cur = ops.mlp_forward(cur, L.w_in, L.b_in, L.w_out, L.b_out, gate, residual=cur, h=h, bits=bits,
+                                  y=bufs[i % 2])
+        return cur
+
+    out = {}
+    for name, fn in (("dff_split", run_split), ("token_sharded", run_tokens)):
+        fn()
+        dist.barrier(device_ids=[device.index])
+        t = max_over_ranks(time_device(fn, steps, device), world, device)
+        out[f"{name}_tokens_per_s"] = world * t_rank / t
+        out[f"{name}_ms_per_step"] = t * 1e3
+    out.update(layers=layers, tokens_per_rank=t_rank, world=world,
+               collective_bytes_per_layer=2 * (world - 1) * t_rank * cfg.d * 2)
+    return out
+
+
 def time_device(fn, steps: int, device) -> float:
     import torch
 
@@ -526,6 +569,8 @@ def run_ours(args):
         "clocks": clocks,
         "device_status": status,
     }
+    if world > 1 and not args.no_extras:
+        line["dff_split_cfg3"] = dff_split_measure(device, world, rank)
     if world == 1 and not args.no_extras:
         import torch
 

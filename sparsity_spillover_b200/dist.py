@@ -114,3 +114,33 @@ def reduce_scatter_tokens(partial: torch.Tensor, world: int, rank: int, group=No
     full = partial.clone()
     dist.all_reduce(full, op=dist.ReduceOp.SUM, group=group)
     return full[rank * per:(rank + 1) * per].contiguous()
+
+
+def all_gather_tokens(shard: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """Concatenate every rank's [T/w, d] token block into the full [T, d] (rank order)."""
+    out = torch.empty((shard.shape[0] * world, shard.shape[1]), dtype=shard.dtype, device=shard.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, shard.contiguous(), group=group)
+    else:
+        parts = [torch.empty_like(shard) for _ in range(world)]
+        dist.all_gather(parts, shard.contiguous(), group=group)
+        torch.cat(parts, out=out)
+    return out
+
+
+def dff_split_forward(layers: list[DffSplitMLP], x: torch.Tensor) -> torch.Tensor:
+    """A stack of d_ff-split layers chained by the parallel residual, x_{l+1} = x_l + MLP_l(x_l).
+
+    x [T, d] is the same on every rank; each layer reduce-scatters its partial
+    down-projection over tokens and the next layer's input is all-gathered again.
+    Returns this rank's [T/w, d] token block of the last layer's output."""
+    if not layers:
+        raise ValueError("need at least one layer")
+    world = dist.get_world_size(layers[0].group)
+    cur = x
+    shard = None
+    for i, layer in enumerate(layers):
+        shard = layer.forward(cur, residual=cur)
+        if i + 1 < len(layers):
+            cur = all_gather_tokens(shard, world, layer.group)
+    return shard

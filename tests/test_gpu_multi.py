@@ -1,0 +1,79 @@
+"""Two-GPU checks (skipped with fewer GPUs): the d_ff split with an NCCL
+reduce-scatter over NVLink matches one GPU within tolerance, and token shards
+are bit-identical to the single-GPU forward of the same tokens."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, queue):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from oracle import mlp as omlp
+        from sparsity_spillover_b200 import dist as sdist
+        from sparsity_spillover_b200 import ops, workloads
+
+        cfg = workloads.CONFIGS["cfg3"]
+        t = 4096
+        full = workloads.make_weights(cfg, dev)[:2]
+        gate = {"operator": "one_sided_threshold", "kappa": 0.5}
+        x = workloads.make_input(cfg, dev, tokens=t)
+        layers = [sdist.DffSplitMLP.from_full(L.w_in, L.b_in, L.w_out, L.b_out, gate, world, rank) for L in full]
+        y_shard = sdist.dff_split_forward(layers, x)
+        # single-GPU reference of the same two layers on this rank's device
+        ref = x
+        for L in full:
+            ref = ops.mlp_forward(ref, L.w_in, L.b_in, L.w_out, L.b_out, gate, residual=ref)
+        lo, hi = rank * t // world, (rank + 1) * t // world
+        err = omlp.max_rel_error(y_shard.float().cpu(), ref[lo:hi].float().cpu())
+        # token sharding: this rank's shard through the unsplit layer equals the full pass's rows
+        tok = ops.mlp_forward(x[lo:hi].contiguous(), full[0].w_in, full[0].b_in, full[0].w_out, full[0].b_out, gate)
+        whole = ops.mlp_forward(x, full[0].w_in, full[0].b_in, full[0].w_out, full[0].b_out, gate)
+        same = bool(torch.equal(tok, whole[lo:hi]))
+        torch.cuda.synchronize(dev)
+        queue.put((rank, err, same, ops.device_status(rank)))
+    finally:
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_dff_split_over_nccl_and_token_shards():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, same, status in results:
+        assert err <= 2e-2, (rank, err)  # fp16 partials summed by NCCL, then bias and residual rounding
+        assert same
+        assert status == 0
