@@ -143,7 +143,12 @@ __device__ __forceinline__ uint32_t kblocks_of_k16(uint32_t m16) {
   return kb;
 }
 
-template <int KIND, int BN, int STAGES, bool BF16, int EPI = 4, int CG = 1>
+// RING = 0: each epilogue warp stages its whole tile (kWarpChunks chunks) in
+// shared memory, and the down projection's residual is TMA-loaded there.
+// RING > 0: each warp cycles through RING single-chunk slots (one TMA store per
+// chunk), and the residual is read into registers; the shared memory saved
+// goes to deeper operand pipelines.
+template <int KIND, int BN, int STAGES, bool BF16, int EPI = 4, int CG = 1, int RING = 0>
 struct GemmTraits {
   static constexpr int kTileM = kBM * CG;                   // tokens per (cluster) tile
   static constexpr uint32_t kABytes = kBM * kBK * 2;         // this CTA's 128 rows of A per stage
@@ -154,9 +159,10 @@ struct GemmTraits {
   static constexpr int kThreads = 64 + 32 * EPI;
   static constexpr uint32_t kStageOutBytes = 32 * 32 * 2;  // one 32-row x 32-column output chunk
   static constexpr int kWarpChunks = (BN / 32) / (EPI / 4);  // chunks one epilogue warp handles per tile
-  static constexpr int kFlush = kWarpChunks < 4 ? kWarpChunks : 4;  // chunks per fence + store batch
-  static constexpr uint32_t kEpiBytes = EPI * kWarpChunks * kStageOutBytes;  // a warp's whole tile slab
-  static constexpr uint32_t kBiasBytes = EPI * BN * 4;
+  static constexpr int kFlush = kWarpChunks < 4 ? kWarpChunks : 4;  // chunks per fence + store batch (RING = 0)
+  static constexpr int kSlabChunks = RING > 0 ? RING : kWarpChunks;  // staged chunks per epilogue warp
+  static constexpr uint32_t kEpiBytes = EPI * kSlabChunks * kStageOutBytes;
+  static constexpr uint32_t kBiasBytes = EPI * kWarpChunks * 32 * 4;  // each warp's own columns, fp32
   static constexpr uint32_t kBarrierBytes = 256;
   static_assert((2 * STAGES + 5 + EPI) * 8 + 4 <= kBarrierBytes, "barrier region too small");
   static constexpr uint32_t kSmemBytes =
@@ -165,6 +171,7 @@ struct GemmTraits {
   static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair");
   static_assert(EPI == 4 || EPI == 8, "4 or 8 epilogue warps");
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
+  static_assert(RING == 0 || (RING >= 2 && RING <= kWarpChunks), "a ring has 2 .. kWarpChunks slots");
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB shared-memory limit");
 };
 
@@ -330,19 +337,19 @@ struct HeadEpilogue {
 // leader's single thread issues tcgen05.mma.cta_group::2 (M = 256) over both
 // CTAs' shared memory, and each CTA's TMEM receives its 128-row half.  Stage
 // completion is counted on the leader's barriers; commits multicast to both.
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG>
-__global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::kThreads, 1)
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0>
+__global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_r,
                       const GemmParams p) {
-  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>;
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
   constexpr int kGroups = Tr::kTileM / kBitsRows;  // 16-row bitmap groups per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + STAGES * Tr::kABytes;
-  uint8_t* s_out = smem + STAGES * Tr::kStageBytes;  // [EPI][kWarpChunks][32x32] staged output chunks
-  float* s_bias = reinterpret_cast<float*>(s_out + Tr::kEpiBytes);  // [EPI][BN]
+  uint8_t* s_out = smem + STAGES * Tr::kStageBytes;  // [EPI][kSlabChunks][32x32] staged output chunks
+  float* s_bias = reinterpret_cast<float*>(s_out + Tr::kEpiBytes);  // [EPI][kWarpChunks * 32]
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_bias) + Tr::kBiasBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]
@@ -363,7 +370,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     tma_prefetch_desc(&tm_c);
-    if (KIND == KIND_DOWN && p.residual != nullptr) tma_prefetch_desc(&tm_r);
+    if (KIND == KIND_DOWN && RING == 0 && p.residual != nullptr) tma_prefetch_desc(&tm_r);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -535,9 +542,11 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
     constexpr int kMyChunks = Tr::kWarpChunks;
     constexpr int kBatches = (kMyChunks + Tr::kFlush - 1) / Tr::kFlush;
     const int ch_begin = (ew / 4) * kMyChunks;  // EPI == 8: the two warps of a quarter split the columns
-    uint8_t* stage_out = s_out + ew * kMyChunks * Tr::kStageOutBytes;
-    float* bias_s = s_bias + ew * BN;
+    constexpr bool kRing = RING > 0;
+    uint8_t* stage_out = s_out + ew * Tr::kSlabChunks * Tr::kStageOutBytes;
+    float* bias_s = s_bias + ew * kMyChunks * 32;  // this warp's columns ch_begin*32 ..
     const bool with_res = KIND == KIND_DOWN && p.residual != nullptr;
+    int ring_slot = 0;  // RING > 0: next slot of this warp's ring (carries across tiles)
     // The accumulator-release barriers live in the leader CTA.
     uint32_t acc_empty_addr[2];
     for (int i = 0; i < 2; ++i)
@@ -569,10 +578,29 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const bool has_acc = live_blocks > 0;
+      const int ch_end = ch_begin + kMyChunks;
+      // RING > 0: the residual of chunk ch (this thread's row, 32 values) into registers.
+      auto load_res = [&](int ch, uint4 (&r)[4]) {
+        if constexpr (kRing && KIND == KIND_DOWN) {
+          const int col0 = n_col0 + ch * 32;
+          if (with_res && row_ok && ch < ch_end && col0 < p.N) {
+            const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.residual) +
+                                                             static_cast<size_t>(row) * p.N + col0);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) r[c] = __ldg(rp + c);
+          }
+        }
+      };
+      // Residual registers of the two chunks in flight, fetched before the accumulator wait.
+      const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+      uint4 res_a[4] = {z4, z4, z4, z4};
+      uint4 res_b[4] = {z4, z4, z4, z4};
+      load_res(ch_begin, res_a);
+      load_res(ch_begin + 1, res_b);
 
       // Residual: TMA it into this warp's output slab while the MMAs run.  The
       // previous tile's stores must first have read the slab.
-      if (with_res) {
+      if (!kRing && with_res) {
         if (lane == 0) {
           bulk_wait_group_read<0>();
           if (row0 < p.M) {
@@ -596,8 +624,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
           float b[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) b[i] = DType<BF16>::to_float(rb[i]);
-          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + lane * 8)[0] = make_float4(b[0], b[1], b[2], b[3]);
-          reinterpret_cast<float4*>(bias_s + ch_begin * 32 + lane * 8)[1] = make_float4(b[4], b[5], b[6], b[7]);
+          reinterpret_cast<float4*>(bias_s + lane * 8)[0] = make_float4(b[0], b[1], b[2], b[3]);
+          reinterpret_cast<float4*>(bias_s + lane * 8)[1] = make_float4(b[4], b[5], b[6], b[7]);
         }
         __syncwarp();
         bias_next = load_bias(t + units);
@@ -609,7 +637,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
         if (!good) break;
         tc_fence_after();
       }
-      if (with_res && row0 < p.M) {
+      if (!kRing && with_res && row0 < p.M) {
         const bool good = __all_sync(0xffffffffu, mbar_wait(&res_full[ew], res_phase, p.status, kDevTimeoutEpilogue));
         res_phase ^= 1u;
         if (!good) break;
@@ -631,11 +659,15 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
 
       uint32_t nz_bits = 0;  // KIND_UP: bit (2*group + half) per 64-column group of the tile
       const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this lane's row in a 32x32 chunk
-      auto process = [&](int ch, const uint32_t (&v)[32]) {
+      auto process = [&](int ch, const uint32_t (&v)[32], const uint4 (&res_regs)[4]) {
         const int col0 = n_col0 + ch * 32;
         const int slot = ch - ch_begin;
-        uint8_t* buf = stage_out + slot * Tr::kStageOutBytes;
-        if (!with_res && slot % Tr::kFlush == 0) {
+        uint8_t* buf = stage_out + (kRing ? ring_slot : slot) * Tr::kStageOutBytes;
+        if constexpr (kRing) {
+          // The store that last used this slot, RING chunks ago, has read it.
+          if (lane == 0) bulk_wait_group_read<(RING > 0 ? RING - 1 : 0)>();
+          __syncwarp();
+        } else if (!with_res && slot % Tr::kFlush == 0) {
           // The store batch that last used these slots has read them.
           if (lane == 0) bulk_wait_group_read<kBatches - 1>();
           __syncwarp();
@@ -644,15 +676,16 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
           uint32_t packed[16];
           bool nz = false;
           if constexpr (KIND == KIND_UP) {
-            nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + ch * 32, k2, packed);
+            nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + slot * 32, k2, packed);
           } else if constexpr (KIND == KIND_DOWN) {
             uint4 r[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
                           make_uint4(0u, 0u, 0u, 0u)};
             if (with_res) {
 #pragma unroll
-              for (int c = 0; c < 4; ++c) r[c] = *reinterpret_cast<const uint4*>(buf + lane * 64 + ((c ^ sw) << 4));
+              for (int c = 0; c < 4; ++c)
+                r[c] = kRing ? res_regs[c] : *reinterpret_cast<const uint4*>(buf + lane * 64 + ((c ^ sw) << 4));
             }
-            DownEpilogue<BF16>::apply(p, v, bias_s + ch * 32, r, packed);
+            DownEpilogue<BF16>::apply(p, v, bias_s + slot * 32, r, packed);
           } else {
             HeadEpilogue<BF16>::apply(v, packed);
           }
@@ -668,8 +701,17 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
             *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
                 make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
         }
-        // Every kFlush chunks: one fence and one batch of TMA stores for the staged chunks.
-        if ((slot + 1) % Tr::kFlush == 0 || slot + 1 == kMyChunks) {
+        if constexpr (kRing) {
+          // One fence and one TMA store per chunk; the slot is reused RING chunks later.
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M && col0 < p.N) tma_store_2d(&tm_c, buf, col0, row0);
+            bulk_commit_group();
+          }
+          ring_slot = ring_slot + 1 == RING ? 0 : ring_slot + 1;
+        } else if ((slot + 1) % Tr::kFlush == 0 || slot + 1 == kMyChunks) {
+          // Every kFlush chunks: one fence and one batch of TMA stores for the staged chunks.
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && row0 < p.M) {
@@ -685,7 +727,6 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
       uint32_t va[32], vb[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) va[j] = vb[j] = 0u;
-      const int ch_end = ch_begin + kMyChunks;
       if (has_acc) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch_begin * 32), va);
 #pragma unroll 1
       for (int ch = ch_begin; ch < ch_end; ch += 2) {
@@ -695,7 +736,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
           if (ch + 1 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 1) * 32), vb);
           if (ch + 1 >= ch_end) release_acc();
         }
-        process(ch, va);
+        process(ch, va, res_a);
+        load_res(ch + 2, res_a);
         if (ch + 1 < ch_end) {
           // odd chunk: vb
           if (has_acc) {
@@ -703,7 +745,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>::k
             if (ch + 2 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 2) * 32), va);
             if (ch + 2 >= ch_end) release_acc();
           }
-          process(ch + 1, vb);
+          process(ch + 1, vb, res_b);
+          load_res(ch + 3, res_b);
         }
       }
       if constexpr (KIND == KIND_UP) {

@@ -43,12 +43,15 @@ int cuda_fail(cudaError_t e, const char* what) {
 constexpr int kMaxDevices = 64;
 
 // Tile configuration of the up-projection: pipeline stages, epilogue warps,
-// staged output chunks per epilogue warp (tuned on B200 for d=512, F=2048).
-constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2;
+// CTAs per tile, output ring slots per epilogue warp (0 = whole-tile slab).
+constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
 // Down-projection, dense and coarse-skip modes: 256-token tiles on CTA pairs.
-constexpr int kDownStages = 4, kDownEpiWarps = 8, kDownCG = 2;
+// Its long reduction (K = d_ff) leaves the epilogue idle most of the time, so
+// four epilogue warps and a two-slot output ring suffice, and the shared memory
+// goes to six operand stages (the loads of h are the bound).
+constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
-constexpr int kDownFineStages = 3, kDownFineEpiWarps = 4;
+constexpr int kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
 
 struct DeviceInfo {
   int sm_count = 0;
@@ -134,11 +137,11 @@ int make_out_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- launch
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG>
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr) {
-  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG>;
-  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG>;
+  using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
+  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING>;
   // Setting the attribute is per function; cheap and idempotent.
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
@@ -188,11 +191,11 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 template <int BN>
 int launch_up(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int gate_op,
               bool bf16, cudaStream_t stream, DeviceInfo* dev) {
-  constexpr int S = kUpStages, E = kUpEpiWarps, C = kUpCG;
-#define SPMLP_UP_CASE(G)                                                                     \
-  case G:                                                                                    \
-    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C>(ta, tb, tc, p, stream, dev)     \
-                : launch_gemm<KIND_UP, G, BN, S, false, E, C>(ta, tb, tc, p, stream, dev);
+  constexpr int S = kUpStages, E = kUpEpiWarps, C = kUpCG, R = kUpRing;
+#define SPMLP_UP_CASE(G)                                                                      \
+  case G:                                                                                     \
+    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev)   \
+                : launch_gemm<KIND_UP, G, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev);
   switch (gate_op) {
     SPMLP_UP_CASE(GATE_IDENTITY)
     SPMLP_UP_CASE(GATE_GELU)
@@ -310,15 +313,15 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   p.bits_words = spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  constexpr int S = kDownStages, E = kDownEpiWarps, C = kDownCG;
-  constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps;
+  constexpr int S = kDownStages, E = kDownEpiWarps, C = kDownCG, R = kDownRing;
+  constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps, RF = kDownFineRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
   if (mode == SPMLP_DOWN_SKIP_FINE) {
-    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, SF, true, EF, 1>(ta, tb, tc, p, stream, dev, trp);
-    return launch_gemm<KIND_DOWN, 0, BN, SF, false, EF, 1>(ta, tb, tc, p, stream, dev, trp);
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp);
+    return launch_gemm<KIND_DOWN, 0, BN, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp);
   }
-  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C>(ta, tb, tc, p, stream, dev, trp);
-  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C>(ta, tb, tc, p, stream, dev, trp);
+  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp);
+  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp);
 }
 
 
