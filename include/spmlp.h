@@ -109,6 +109,38 @@ int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_ou
                       const void* residual, void* y, int64_t T, int F, int d, int dtype, int mode,
                       uint64_t* stats, void* stream);
 
+/* Joint consumer: the MLP's down projection and the attention output
+ * projection of one GPT-NeoX layer, summed with its parallel residual, in one
+ * kernel.  Replaces the reference's joint (the k018 Joint.__call__ of
+ * runs/026-2026-09-06-pythia14m-fused-sparse-kernel/autoresearch/candidates/k018/candidate.py:32-46
+ * called from layer_forward :48-56, and the K042 kernel
+ * runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:88-137 behind
+ * runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/candidate.py:26-33).
+ *   h [T,F] with tile_bits (ignored for SPMLP_DOWN_DENSE), z [T,d] (the
+ *   attention context before its dense projection), w2 [d,F], b2 [d], wo [d,d],
+ *   bo [d] (biases nullable), residual [T,d] (nullable) -> out [T,d]
+ *   out = round(round(round(h w2^T + b2) + round(z wo^T + bo)) + residual),
+ *   every addition in fp32: the rounding order of
+ *   runs/027-2026-09-06-pythia14m-kernel-sparsity-characterization/test_adapter.py:19-24
+ *   and runs/042-2026-09-20-pythia70m-sparse-scale/controls.py:19-26.
+ *   The reference's input gates (h < th and z < tz set to zero) are applied
+ *   beforehand with spmlp_gate.  mode and stats as spmlp_down_sparse (over the
+ *   h branch; z is dense); output tiles are spmlp_down_tile_tokens(mode) x 128. */
+int spmlp_joint(const void* h, const uint32_t* tile_bits, const void* z, const void* w2, const void* b2,
+                const void* wo, const void* bo, const void* residual, void* out, int64_t T, int F, int d,
+                int dtype, int mode, uint64_t* stats, void* stream);
+
+/* Elementwise gate of an activation x [T,F] into out (the same buffer, or one
+ * that does not overlap it), and, when tile_bits is non-null, the 16x64 tile
+ * bitmap of the gated values (layout as spmlp_up_gate's).  gate_op is one of
+ * SPMLP_GATE_IDENTITY, _ONE_SIDED, _SYMMETRIC, _RELU with kappa rounded to
+ * dtype: the reference's FixedOneSidedThreshold / FixedSymmetricThreshold /
+ * ReLU (src/sparsity_research/sites.py:86-107, 221-222) as the joint consumer
+ * applies them to its h and z inputs (runs/042-2026-09-20-pythia70m-sparse-scale/controls.py:20-23).
+ * F must be a positive multiple of 64. */
+int spmlp_gate(const void* x, void* out, uint32_t* tile_bits, int64_t T, int F, int dtype, int gate_op,
+               float kappa, void* stream);
+
 /* Whole gated MLP forward: spmlp_up_gate then spmlp_down_sparse, with the
  * caller's h and tile-bit buffers as workspace (GPTNeoXMLP.forward). */
 int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const void* w_out,

@@ -4,7 +4,8 @@ A drop-in for the reference's gated MLP hot path (thiagocmattar/sparsity-spillov
 
 * ``ops``       tensor-level entry points over the C ABI of ``libspmlp.so``
                 (``include/spmlp.h``) and ``torch.ops.spmlp.*`` registrations;
-* ``mlp``       ``SparseGPTNeoXMLP`` / ``SparseHead`` modules and ``install(model)``;
+* ``mlp``       ``SparseGPTNeoXMLP`` / ``SparseHead`` modules, ``install(model)``, the
+                joint consumer ``JointConsumer`` and ``install_joint(model)``;
 * ``gates``     the reference's gate specs and modules -> kernel gate enum;
 * ``workloads`` seeded synthetic inputs of the benchmark configs;
 * ``dist``      token sharding and the d_ff split with an NCCL reduce-scatter.
@@ -13,11 +14,12 @@ Every compute call goes through libspmlp.so; there is no CPU fallback.
 """
 from __future__ import annotations
 
-__all__ = ["ops", "mlp", "gates", "workloads", "SparseGPTNeoXMLP", "SparseHead", "install"]
+__all__ = ["ops", "mlp", "gates", "workloads", "SparseGPTNeoXMLP", "SparseHead", "install", "JointConsumer",
+           "install_joint"]
 
 
 def __getattr__(name):
-    if name in ("SparseGPTNeoXMLP", "SparseHead", "install"):
+    if name in ("SparseGPTNeoXMLP", "SparseHead", "install", "JointConsumer", "install_joint"):
         from . import mlp
 
         return getattr(mlp, name)

@@ -8,6 +8,8 @@
 
 #include <stdint.h>
 
+#include "gemm_sm100.cuh"
+
 namespace spmlp {
 
 // One CTA per 16-row group; each warp scans whole 16x64 tiles: lane l reads the
@@ -36,6 +38,64 @@ __global__ void __launch_bounds__(256) tile_bits_kernel(const uint16_t* __restri
   }
   __syncthreads();
   for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
+}
+
+// Elementwise gate of an activation x [T, F] into out (which may alias x), and
+// optionally the 16x64 tile bitmap of the gated values.  Gates: identity, one-
+// sided (keep z >= kappa), symmetric (keep |z| >= kappa), ReLU -- the same packed
+// comparisons as the up-projection epilogue, so NaN is kept and -0.0 counts as
+// zero.  This serves inputs gated outside the up projection: the joint
+// consumer's h and attention-output z branches.  Same grid as tile_bits_kernel.
+template <bool BF16>
+__global__ void __launch_bounds__(256) gate_bits_kernel(const uint16_t* x, uint16_t* out, uint32_t* __restrict__ bits,
+                                                        int T, int F, int words, int gate_op, float kappa) {
+  using D = DType<BF16>;
+  extern __shared__ uint32_t s_words[];
+  const int rg = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  if (bits != nullptr) {
+    for (int w = threadIdx.x; w < words; w += blockDim.x) s_words[w] = 0u;
+    __syncthreads();
+  }
+  const uint32_t k2 = D::pack_rn(kappa, kappa);  // exact: kappa is already a dtype value
+  auto gate = [&](uint32_t w) -> uint32_t {
+    switch (gate_op) {
+      case GATE_ONE_SIDED:
+        return w & ~D::lt_mask(w, k2);
+      case GATE_SYMMETRIC:
+        return w & ~D::lt_mask(w & 0x7fff7fffu, k2);
+      case GATE_RELU:
+        return w & ~D::lt_mask(w, 0u);
+      default:
+        return w;
+    }
+  };
+  const int tiles = F / 64;
+  const int row = rg * 16 + (lane >> 1);
+  for (int g = warp; g < tiles; g += nwarps) {
+    uint32_t acc = 0;
+    if (row < T) {
+      const size_t off = static_cast<size_t>(row) * F + g * 64 + (lane & 1) * 32;
+      const uint4* src = reinterpret_cast<const uint4*>(x + off);
+      uint4* dst = reinterpret_cast<uint4*>(out + off);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 v = __ldcs(src + i);
+        v.x = gate(v.x);
+        v.y = gate(v.y);
+        v.z = gate(v.z);
+        v.w = gate(v.w);
+        dst[i] = v;
+        acc |= (v.x | v.y | v.z | v.w) & 0x7fff7fffu;
+      }
+    }
+    if (bits != nullptr && __any_sync(0xffffffffu, acc != 0) && lane == 0) atomicOr(&s_words[g >> 5], 1u << (g & 31));
+  }
+  if (bits != nullptr) {
+    __syncthreads();
+    for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
+  }
 }
 
 }  // namespace spmlp

@@ -22,6 +22,10 @@
 //   KIND_HEAD  logits = round(acc) over an explicit list of active 128-column
 //              vocabulary tiles, optionally skipping dead K16 groups of the
 //              head input (corner certificates).        (GPTNeoXForCausalLM.embed_out)
+//   KIND_JOINT out = round(round(round(h W2^T + b2) + round(z Wo^T + bo)) + r):
+//              the MLP's down projection (tile-skipping over h) and the
+//              attention output projection in two TMEM accumulators of the
+//              same tile, with GPT-NeoX's parallel residual.  (the joint consumer)
 #pragma once
 
 #include <cuda_bf16.h>
@@ -31,7 +35,7 @@
 
 namespace spmlp {
 
-enum Kind : int { KIND_UP = 0, KIND_DOWN = 1, KIND_HEAD = 2 };
+enum Kind : int { KIND_UP = 0, KIND_DOWN = 1, KIND_HEAD = 2, KIND_JOINT = 3 };
 
 // Gate operators applied to the rounded up-projection output z.
 enum GateOp : int {
@@ -55,9 +59,11 @@ struct GemmParams {
   const void* bias;       // [N] in the activation dtype, nullable
   void* out;              // [M, N] row-major output (h, y or logits)
   void* z_out;            // KIND_UP: optional pre-gate z [M, N]
-  const void* residual;   // KIND_DOWN: optional [M, N]
+  const void* residual;   // KIND_DOWN / KIND_JOINT: optional [M, N]
+  int K2;                 // KIND_JOINT: reduction length of the second product (z Wo^T)
+  const void* bias2;      // KIND_JOINT: [N] bias of the second product, nullable
   uint32_t* bits_out;     // KIND_UP: 16x64 tile bitmap, zeroed by the host
-  const uint32_t* bits_in;  // KIND_DOWN: 16x64 bitmap; KIND_HEAD: 16x16 support bits
+  const uint32_t* bits_in;  // KIND_DOWN / KIND_JOINT: 16x64 bitmap of A; KIND_HEAD: 16x16 support bits
   int bits_words;         // words per 16-row group in bits_out / bits_in
   int skip;               // KIND_DOWN/HEAD: 1 = skip dead K granules
   const int* col_tiles;   // KIND_HEAD: active BN-column tile indices
@@ -154,7 +160,9 @@ struct GemmTraits {
   static constexpr uint32_t kABytes = kBM * kBK * 2;         // this CTA's 128 rows of A per stage
   static constexpr uint32_t kBBytes = (BN / CG) * kBK * 2;   // this CTA's share of B per stage
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator (this CTA's M half)
+  static constexpr int kAccs = KIND == KIND_JOINT ? 2 : 1;     // accumulators per tile
+  static constexpr uint32_t kAccCols = kAccs * BN;               // TMEM columns of one tile's accumulators
+  static constexpr uint32_t kTmemCols = 2 * kAccCols;  // double-buffered (this CTA's M half)
   static constexpr int kEpiWarps = EPI;          // 4: one warp per TMEM lane quarter; 8: two, splitting columns
   static constexpr int kThreads = 64 + 32 * EPI;
   static constexpr uint32_t kStageOutBytes = 32 * 32 * 2;  // one 32-row x 32-column output chunk
@@ -162,7 +170,7 @@ struct GemmTraits {
   static constexpr int kFlush = kWarpChunks < 4 ? kWarpChunks : 4;  // chunks per fence + store batch (RING = 0)
   static constexpr int kSlabChunks = RING > 0 ? RING : kWarpChunks;  // staged chunks per epilogue warp
   static constexpr uint32_t kEpiBytes = EPI * kSlabChunks * kStageOutBytes;
-  static constexpr uint32_t kBiasBytes = EPI * kWarpChunks * 32 * 4;  // each warp's own columns, fp32
+  static constexpr uint32_t kBiasBytes = kAccs * EPI * kWarpChunks * 32 * 4;  // each warp's own columns, fp32
   static constexpr uint32_t kBarrierBytes = 256;
   static_assert((2 * STAGES + 5 + EPI) * 8 + 4 <= kBarrierBytes, "barrier region too small");
   static constexpr uint32_t kSmemBytes =
@@ -331,6 +339,29 @@ struct HeadEpilogue {
   }
 };
 
+// The joint consumer in the reference's rounding order (torch's bf16/fp16 ops):
+// a = round(acc_h + b2), b = round(acc_z + bo), s = round(a + b), out = round(s + r),
+// every addition in fp32.
+template <bool BF16>
+struct JointEpilogue {
+  using D = DType<BF16>;
+  __device__ __forceinline__ static void apply(const uint32_t (&acc_h)[32], const uint32_t (&acc_z)[32],
+                                               const float* bias_h, const float* bias_z, const uint4 (&res)[4],
+                                               bool with_res, uint32_t (&out)[16]) {
+    const uint32_t* r = reinterpret_cast<const uint32_t*>(&res[0]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t a = D::pack_rn(__uint_as_float(acc_h[2 * j]) + bias_h[2 * j],
+                                    __uint_as_float(acc_h[2 * j + 1]) + bias_h[2 * j + 1]);
+      const uint32_t b = D::pack_rn(__uint_as_float(acc_z[2 * j]) + bias_z[2 * j],
+                                    __uint_as_float(acc_z[2 * j + 1]) + bias_z[2 * j + 1]);
+      uint32_t sum = D::pack_rn(D::lo(a) + D::lo(b), D::hi(a) + D::hi(b));
+      if (with_res) sum = D::pack_rn(D::lo(sum) + D::lo(r[j]), D::hi(sum) + D::hi(r[j]));
+      out[j] = sum;
+    }
+  }
+};
+
 // ------------------------------------------------------------------ kernel
 // CG = 1: one CTA per 128 x BN tile.  CG = 2: a CTA pair (cluster of 2) per
 // 256 x BN tile: each CTA loads its 128 rows of A and BN/2 rows of B, the
@@ -341,6 +372,7 @@ template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, in
 __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_r,
+                      const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_b2,
                       const GemmParams p) {
   using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
   constexpr int kGroups = Tr::kTileM / kBitsRows;  // 16-row bitmap groups per tile
@@ -370,7 +402,11 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     tma_prefetch_desc(&tm_c);
-    if (KIND == KIND_DOWN && RING == 0 && p.residual != nullptr) tma_prefetch_desc(&tm_r);
+    if ((KIND == KIND_DOWN || KIND == KIND_JOINT) && RING == 0 && p.residual != nullptr) tma_prefetch_desc(&tm_r);
+    if (KIND == KIND_JOINT) {
+      tma_prefetch_desc(&tm_a2);
+      tma_prefetch_desc(&tm_b2);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -404,21 +440,22 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       tile_coords<KIND, BN>(p, t, m_blk, n_col0);
       const int a_row = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM;
       const int b_row = n_col0 + static_cast<int>(rank) * (BN / CG);
-      ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int kb, uint32_t) {
+      // Load K-block kb of (ma, mb) into the next ring stage (warp-collective).
+      auto issue = [&](const CUtensorMap* ma, const CUtensorMap* mb, int kb) -> bool {
         bool good = true;
         if (lane == 0) {
           good = mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutProducer);
           if (good) {
             if constexpr (CG == 1) {
               mbar_arrive_expect_tx(&full[stage], Tr::kStageBytes);
-              tma_load_2d(s_a + stage * Tr::kABytes, &tm_a, &full[stage], kb * kBK, a_row, 0ull);
-              tma_load_2d(s_b + stage * Tr::kBBytes, &tm_b, &full[stage], kb * kBK, b_row, pol_b);
+              tma_load_2d(s_a + stage * Tr::kABytes, ma, &full[stage], kb * kBK, a_row, 0ull);
+              tma_load_2d(s_b + stage * Tr::kBBytes, mb, &full[stage], kb * kBK, b_row, pol_b);
             } else {
               // Both CTAs' bytes land on the leader's barrier; only the leader arrives.
               if (leader) mbar_arrive_expect_tx(&full[stage], CG * Tr::kStageBytes);
               const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-              tma_load_2d_pair(s_a + stage * Tr::kABytes, &tm_a, bar, kb * kBK, a_row, 0ull);
-              tma_load_2d_pair(s_b + stage * Tr::kBBytes, &tm_b, bar, kb * kBK, b_row, pol_b);
+              tma_load_2d_pair(s_a + stage * Tr::kABytes, ma, bar, kb * kBK, a_row, 0ull);
+              tma_load_2d_pair(s_b + stage * Tr::kBBytes, mb, bar, kb * kBK, b_row, pol_b);
             }
           }
         }
@@ -431,7 +468,14 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           }
         }
         return good;
-      });
+      };
+      if constexpr (KIND == KIND_JOINT) {
+        // The attention-output branch first: every K-block of z and Wo.
+        for (int kb = 0; kb < p.K2 / kBK && ok; ++kb) ok = issue(&tm_a2, &tm_b2, kb);
+        if (!ok) break;
+      }
+      ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane,
+                                               [&](int kb, uint32_t) { return issue(&tm_a, &tm_b, kb); });
     }
     if (!ok && lane == 0) {
       // Error path: let the copies this warp started land before the CTA exits.
@@ -477,14 +521,16 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
         skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
         issued_steps += static_cast<unsigned long long>(live_steps);
-        if (live_blocks == 0) continue;  // the epilogue writes the zero-accumulator result itself
+        // A tile without live K-blocks needs no MMA: the epilogue writes the
+        // zero-accumulator result itself (the joint always has its z branch).
+        if (KIND != KIND_JOINT && live_blocks == 0) continue;
         if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        uint32_t accumulate = 0;
-        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int, uint32_t k16) {
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * Tr::kAccCols;
+        // MMAs of the next ring stage into accumulator d (warp-collective).
+        auto mma_stage = [&](uint32_t d, uint32_t k16, uint32_t& accumulate) -> bool {
           bool good = true;
           if (lane == 0) {
             good = mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma);
@@ -496,8 +542,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
               for (int k = 0; k < kBK / 16; ++k) {
                 if ((k16 >> k) & 1u) {
                   // +32 bytes per K16 step inside the 128-byte swizzled row (>>4 encoded)
-                  umma_f16<CG>(d_tmem, a_desc + static_cast<uint64_t>(2 * k), b_desc + static_cast<uint64_t>(2 * k),
-                               idesc, accumulate);
+                  umma_f16<CG>(d, a_desc + static_cast<uint64_t>(2 * k), b_desc + static_cast<uint64_t>(2 * k), idesc,
+                               accumulate);
                   accumulate = 1;
                 }
               }
@@ -510,7 +556,16 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
             phase ^= 1u;
           }
           return good;
-        });
+        };
+        if constexpr (KIND == KIND_JOINT) {
+          // z Wo^T into the second accumulator, in the order the producer loaded it.
+          uint32_t accumulate_z = 0;
+          for (int kb = 0; kb < p.K2 / kBK && ok; ++kb) ok = mma_stage(d_tmem + BN, 0xFu, accumulate_z);
+          if (!ok) break;
+        }
+        uint32_t accumulate = 0;
+        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane,
+                                                 [&](int, uint32_t k16) { return mma_stage(d_tmem, k16, accumulate); });
         if (!ok) break;
         if (lane == 0) umma_commit<CG>(&acc_full[acc]);
         __syncwarp();
@@ -545,7 +600,9 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     constexpr bool kRing = RING > 0;
     uint8_t* stage_out = s_out + ew * Tr::kSlabChunks * Tr::kStageOutBytes;
     float* bias_s = s_bias + ew * kMyChunks * 32;  // this warp's columns ch_begin*32 ..
-    const bool with_res = KIND == KIND_DOWN && p.residual != nullptr;
+    float* bias2_s = bias_s + EPI * kMyChunks * 32;  // KIND_JOINT: the second product's bias
+    constexpr bool kHasRes = KIND == KIND_DOWN || KIND == KIND_JOINT;
+    const bool with_res = kHasRes && p.residual != nullptr;
     int ring_slot = 0;  // RING > 0: next slot of this warp's ring (carries across tiles)
     // The accumulator-release barriers live in the leader CTA.
     uint32_t acc_empty_addr[2];
@@ -556,18 +613,28 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     const uint32_t k2 = DType<BF16>::pack_rn(p.kappa, p.kappa);  // kappa in both halves (exact: pre-rounded)
 
     // Bias of one tile's columns for this warp: lane l holds 8 values (one 16-byte vector).
-    const bool bias_lane = KIND != KIND_HEAD && p.bias != nullptr && lane * 8 < kMyChunks * 32;
-    auto load_bias = [&](int t) -> uint4 {
+    const bool bias_lane = KIND != KIND_HEAD && lane * 8 < kMyChunks * 32;
+    auto load_bias = [&](const void* bias, int t) -> uint4 {
       uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-      if (bias_lane && t < total_tiles) {
+      if (bias_lane && bias != nullptr && t < total_tiles) {
         int mb, nc;
         tile_coords<KIND, BN>(p, t, mb, nc);
         const int col = nc + ch_begin * 32 + lane * 8;
-        if (col < p.N) raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.bias) + col));
+        if (col < p.N) raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(bias) + col));
       }
       return raw;
     };
-    uint4 bias_next = load_bias(unit);
+    // Eight packed dtype values -> eight fp32 values at dst.
+    auto store_bias = [&](const uint4& raw, float* dst) {
+      const uint16_t* hb = reinterpret_cast<const uint16_t*>(&raw);
+      float b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) b[i] = DType<BF16>::to_float(hb[i]);
+      reinterpret_cast<float4*>(dst)[0] = make_float4(b[0], b[1], b[2], b[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(b[4], b[5], b[6], b[7]);
+    };
+    uint4 bias_next = load_bias(p.bias, unit);
+    uint4 bias2_next = KIND == KIND_JOINT ? load_bias(p.bias2, unit) : make_uint4(0u, 0u, 0u, 0u);
 
     for (int t = unit; t < total_tiles; t += units) {
       int m_blk, n_col0;
@@ -577,11 +644,12 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const int row0 = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
-      const bool has_acc = live_blocks > 0;
+      const bool has_acc = KIND == KIND_JOINT || live_blocks > 0;  // the joint's z branch is never empty
+      const bool has_h = live_blocks > 0;                             // KIND_JOINT: the h accumulator was written
       const int ch_end = ch_begin + kMyChunks;
       // RING > 0: the residual of chunk ch (this thread's row, 32 values) into registers.
       auto load_res = [&](int ch, uint4 (&r)[4]) {
-        if constexpr (kRing && KIND == KIND_DOWN) {
+        if constexpr (kRing && kHasRes) {
           const int col0 = n_col0 + ch * 32;
           if (with_res && row_ok && ch < ch_end && col0 < p.N) {
             const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.residual) +
@@ -620,15 +688,12 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       if constexpr (KIND != KIND_HEAD) {
         __syncwarp();  // every lane is done with the previous tile's bias
         if (lane * 8 < kMyChunks * 32) {
-          const uint16_t* rb = reinterpret_cast<const uint16_t*>(&bias_next);
-          float b[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) b[i] = DType<BF16>::to_float(rb[i]);
-          reinterpret_cast<float4*>(bias_s + lane * 8)[0] = make_float4(b[0], b[1], b[2], b[3]);
-          reinterpret_cast<float4*>(bias_s + lane * 8)[1] = make_float4(b[4], b[5], b[6], b[7]);
+          store_bias(bias_next, bias_s + lane * 8);
+          if constexpr (KIND == KIND_JOINT) store_bias(bias2_next, bias2_s + lane * 8);
         }
         __syncwarp();
-        bias_next = load_bias(t + units);
+        bias_next = load_bias(p.bias, t + units);
+        if constexpr (KIND == KIND_JOINT) bias2_next = load_bias(p.bias2, t + units);
       }
 
       if (has_acc) {
@@ -643,7 +708,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         if (!good) break;
       }
       const uint32_t t_row =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc) * Tr::kAccCols;
 
       // Release the accumulator (once per warp) when its last TMEM load completed.
       auto release_acc = [&]() {
@@ -659,7 +724,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
 
       uint32_t nz_bits = 0;  // KIND_UP: bit (2*group + half) per 64-column group of the tile
       const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this lane's row in a 32x32 chunk
-      auto process = [&](int ch, const uint32_t (&v)[32], const uint4 (&res_regs)[4]) {
+      // v: the chunk's accumulator values (KIND_JOINT: of h W2^T, with v2 those of z Wo^T).
+      auto process = [&](int ch, const uint32_t (&v)[32], const uint32_t (&v2)[32], const uint4 (&res_regs)[4]) {
         const int col0 = n_col0 + ch * 32;
         const int slot = ch - ch_begin;
         uint8_t* buf = stage_out + (kRing ? ring_slot : slot) * Tr::kStageOutBytes;
@@ -686,6 +752,15 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
                 r[c] = kRing ? res_regs[c] : *reinterpret_cast<const uint4*>(buf + lane * 64 + ((c ^ sw) << 4));
             }
             DownEpilogue<BF16>::apply(p, v, bias_s + slot * 32, r, packed);
+          } else if constexpr (KIND == KIND_JOINT) {
+            const uint4 z4r = make_uint4(0u, 0u, 0u, 0u);
+            uint4 r[4] = {z4r, z4r, z4r, z4r};
+            if (with_res) {
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                r[c] = kRing ? res_regs[c] : *reinterpret_cast<const uint4*>(buf + lane * 64 + ((c ^ sw) << 4));
+            }
+            JointEpilogue<BF16>::apply(v, v2, bias_s + slot * 32, bias2_s + slot * 32, r, with_res, packed);
           } else {
             HeadEpilogue<BF16>::apply(v, packed);
           }
@@ -724,29 +799,53 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         }
       };
 
-      uint32_t va[32], vb[32];
+      if constexpr (KIND == KIND_JOINT) {
+        // Two accumulators per chunk: h W2^T at t_row, z Wo^T at t_row + BN.
+        auto joint_chunk = [&](int ch, const uint4 (&res_regs)[4]) {
+          uint32_t vh[32], vz[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) va[j] = vb[j] = 0u;
-      if (has_acc) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch_begin * 32), va);
+          for (int j = 0; j < 32; ++j) vh[j] = 0u;  // h without live K-blocks contributes zero
+          if (has_h) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch * 32), vh);
+          tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(BN + ch * 32), vz);
+          tmem_wait_ld(vz);
+          tmem_pin(vh);
+          if (ch + 1 == ch_end) release_acc();
+          process(ch, vh, vz, res_regs);
+        };
 #pragma unroll 1
-      for (int ch = ch_begin; ch < ch_end; ch += 2) {
-        // even chunk: va
-        if (has_acc) {
-          tmem_wait_ld(va);
-          if (ch + 1 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 1) * 32), vb);
-          if (ch + 1 >= ch_end) release_acc();
-        }
-        process(ch, va, res_a);
-        load_res(ch + 2, res_a);
-        if (ch + 1 < ch_end) {
-          // odd chunk: vb
-          if (has_acc) {
-            tmem_wait_ld(vb);
-            if (ch + 2 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 2) * 32), va);
-            if (ch + 2 >= ch_end) release_acc();
+        for (int ch = ch_begin; ch < ch_end; ch += 2) {
+          joint_chunk(ch, res_a);
+          load_res(ch + 2, res_a);
+          if (ch + 1 < ch_end) {
+            joint_chunk(ch + 1, res_b);
+            load_res(ch + 3, res_b);
           }
-          process(ch + 1, vb, res_b);
-          load_res(ch + 3, res_b);
+        }
+      } else {
+        uint32_t va[32], vb[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) va[j] = vb[j] = 0u;
+        if (has_acc) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(ch_begin * 32), va);
+#pragma unroll 1
+        for (int ch = ch_begin; ch < ch_end; ch += 2) {
+          // even chunk: va
+          if (has_acc) {
+            tmem_wait_ld(va);
+            if (ch + 1 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 1) * 32), vb);
+            if (ch + 1 >= ch_end) release_acc();
+          }
+          process(ch, va, va, res_a);
+          load_res(ch + 2, res_a);
+          if (ch + 1 < ch_end) {
+            // odd chunk: vb
+            if (has_acc) {
+              tmem_wait_ld(vb);
+              if (ch + 2 < ch_end) tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>((ch + 2) * 32), va);
+              if (ch + 2 >= ch_end) release_acc();
+            }
+            process(ch + 1, vb, vb, res_b);
+            load_res(ch + 3, res_b);
+          }
         }
       }
       if constexpr (KIND == KIND_UP) {

@@ -291,6 +291,19 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[32]) {
       : "memory");
 }
 
+// Orders later reads of `v` after a tcgen05.wait::ld issued for other registers
+// (emits no instruction).
+__device__ __forceinline__ void tmem_pin(uint32_t (&v)[32]) {
+  asm volatile(""
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                 "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]),
+                 "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]),
+                 "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+               :
+               : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with
 // 128-byte swizzling: rows of 64 fp16/bf16 (128 B), 8-row swizzle atoms of 1 KiB.
 // Fields: start address >> 4 (bits 0-13), leading byte offset >> 4 (16-29, unused

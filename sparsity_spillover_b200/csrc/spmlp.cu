@@ -52,6 +52,9 @@ constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
 constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
 constexpr int kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
+// Joint consumer: 128 output columns per tile so that both accumulators of a
+// tile fit twice in TMEM (2 x 2 x 128 columns); 24 KB (pair) / 32 KB stages.
+constexpr int kJointBN = 128, kJointStages = 8, kJointFineStages = 6, kJointEpiWarps = 4, kJointRing = 2;
 
 struct DeviceInfo {
   int sm_count = 0;
@@ -139,7 +142,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // ---------------------------------------------------------------- launch
 template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
-                cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr) {
+                cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr,
+                const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
   using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
   auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING>;
   // Setting the attribute is per function; cheap and idempotent.
@@ -180,7 +184,8 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   }
   if (tiles < units) units = tiles;
   cfg.gridDim = dim3(units * CG);
-  e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr != nullptr ? *tr : tc, p);
+  e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr != nullptr ? *tr : tc, ta2 != nullptr ? *ta2 : ta,
+                         tb2 != nullptr ? *tb2 : tb, p);
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -324,6 +329,90 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp);
 }
 
+int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w2, const void* b2, const void* wo,
+               const void* bo, const void* residual, void* out, int64_t T, int F, int d, int dtype, int mode,
+               uint64_t* stats, cudaStream_t stream) {
+  int rc;
+  if (!h || !z || !w2 || !wo || !out) return fail(SPMLP_EINVAL, "h, z, w2, wo and out must be non-null");
+  if (mode != SPMLP_DOWN_DENSE && mode != SPMLP_DOWN_SKIP && mode != SPMLP_DOWN_SKIP_FINE)
+    return fail(SPMLP_EINVAL, "unknown joint mode %d", mode);
+  if (mode != SPMLP_DOWN_DENSE && !bits) return fail(SPMLP_EINVAL, "the skipping joint modes need tile_bits");
+  if ((rc = check_dtype(dtype))) return rc;
+  if ((rc = check_mk(T, F, d, "F", "d"))) return rc;
+  if (!aligned16(h) || !aligned16(z) || !aligned16(w2) || !aligned16(wo) || !aligned16(out) ||
+      (b2 && !aligned16(b2)) || (bo && !aligned16(bo)) || (residual && !aligned16(residual)))
+    return fail(SPMLP_EALIGN, "h, z, w2, b2, wo, bo, residual and out must be 16-byte aligned");
+  if (stats && (reinterpret_cast<uintptr_t>(stats) & 7u)) return fail(SPMLP_EALIGN, "stats must be 8-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const bool bf16 = dtype == SPMLP_BF16;
+  constexpr int BN = kJointBN;
+  const int cg = mode == SPMLP_DOWN_SKIP_FINE ? 1 : 2;
+  CUtensorMap ta, tb, ta2, tb2, tc, tr;
+  if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb, w2, d, F, BN / cg, bf16))) return rc;
+  if ((rc = make_kmajor_map(&ta2, z, T, d, kBM, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb2, wo, d, d, BN / cg, bf16))) return rc;
+  if ((rc = make_out_map(&tc, out, T, d, bf16))) return rc;
+  if (residual != nullptr && (rc = make_out_map(&tr, residual, T, d, bf16))) return rc;
+  GemmParams p{};
+  p.M = static_cast<int>(T);
+  p.N = d;
+  p.K = F;
+  p.K2 = d;
+  p.n_tiles = (d + BN - 1) / BN;
+  p.bias = b2;
+  p.bias2 = bo;
+  p.out = out;
+  p.residual = residual;
+  p.bits_in = bits;
+  p.bits_words = spmlp_tile_bits_words(F);
+  p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
+  p.stats = reinterpret_cast<unsigned long long*>(stats);
+  constexpr int E = kJointEpiWarps, R = kJointRing;
+  const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
+  if (mode == SPMLP_DOWN_SKIP_FINE) {
+    constexpr int S = kJointFineStages;
+    if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+    return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+  }
+  constexpr int S = kJointStages;
+  if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+  return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+}
+
+int gate_impl(const void* x, void* out, uint32_t* bits, int64_t T, int F, int dtype, int gate_op, float kappa,
+              cudaStream_t stream) {
+  int rc;
+  if (!x || !out) return fail(SPMLP_EINVAL, "x and out must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (gate_op != SPMLP_GATE_IDENTITY && gate_op != SPMLP_GATE_ONE_SIDED && gate_op != SPMLP_GATE_SYMMETRIC &&
+      gate_op != SPMLP_GATE_RELU)
+    return fail(SPMLP_EINVAL, "spmlp_gate takes the identity, one-sided, symmetric or ReLU gate (got %d)", gate_op);
+  if (!std::isfinite(kappa) || kappa < 0.f) return fail(SPMLP_EINVAL, "kappa must be a finite nonnegative number");
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T must be in [1, 2^31)");
+  if (F < kBitsCols || F % kBitsCols) return fail(SPMLP_ESHAPE, "F=%d must be a positive multiple of 64", F);
+  if (!aligned16(x) || !aligned16(out)) return fail(SPMLP_EALIGN, "x and out must be 16-byte aligned");
+  if (x != out) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(x), b = reinterpret_cast<uintptr_t>(out);
+    const uintptr_t n = static_cast<uintptr_t>(T) * F * 2;
+    if (a < b + n && b < a + n) return fail(SPMLP_EINVAL, "x and out must be the same buffer or not overlap");
+  }
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int words = spmlp_tile_bits_words(F);
+  const int groups = static_cast<int>((T + kBitsRows - 1) / kBitsRows);
+  const size_t smem = bits != nullptr ? static_cast<size_t>(words) * 4 : 0;
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  uint16_t* os = static_cast<uint16_t*>(out);
+  if (dtype == SPMLP_BF16)
+    gate_bits_kernel<true><<<groups, 256, smem, stream>>>(xs, os, bits, static_cast<int>(T), F, words, gate_op, kappa);
+  else
+    gate_bits_kernel<false><<<groups, 256, smem, stream>>>(xs, os, bits, static_cast<int>(T), F, words, gate_op, kappa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gate_bits_kernel launch");
+  return 0;
+}
 
 int tile_bits_impl(const void* h, uint32_t* bits, int64_t T, int F, int dtype, cudaStream_t stream) {
   int rc;
@@ -530,6 +619,18 @@ int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_ou
                       void* stream) {
   return down_impl(h, tile_bits, w_out, b_out, residual, y, T, F, d, dtype, mode, stats,
                    static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_joint(const void* h, const uint32_t* tile_bits, const void* z, const void* w2, const void* b2,
+                const void* wo, const void* bo, const void* residual, void* out, int64_t T, int F, int d, int dtype,
+                int mode, uint64_t* stats, void* stream) {
+  return joint_impl(h, tile_bits, z, w2, b2, wo, bo, residual, out, T, F, d, dtype, mode, stats,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_gate(const void* x, void* out, uint32_t* tile_bits, int64_t T, int F, int dtype, int gate_op, float kappa,
+               void* stream) {
+  return gate_impl(x, out, tile_bits, T, F, dtype, gate_op, kappa, static_cast<cudaStream_t>(stream));
 }
 
 int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const void* w_out, const void* b_out,

@@ -11,6 +11,15 @@ and reused across calls, like the reference adapters' preallocated outputs
 ``SparseHead`` replaces ``embed_out`` (runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/
 inference/head.py:53-90).
 
+``JointConsumer`` replaces the reference's joint consumer of a parallel-residual
+layer (``Joint`` of runs/026-2026-09-06-pythia14m-fused-sparse-kernel/autoresearch/
+candidates/k018/candidate.py:25-46 and runs/027-2026-09-06-pythia14m-kernel-sparsity-
+characterization/adapter.py:35-51): ``joint(h, z, residual)`` returns
+``round(round(round(W2 h + b2) + round(Wo z + bo)) + residual)`` with the h and z
+gates applied first.  ``install_joint(model)`` rewires every layer's forward the way
+the reference's adapter does (k018 candidate.py:48-56, 69-75), with the up projection,
+gate and bitmap fused by ``up_gate``.
+
 Both are inference-only and CUDA-only: they raise under autograd or on CPU
 tensors, as the reference adapters do (candidate.py:27).
 """
@@ -20,7 +29,9 @@ from typing import Any
 
 import torch
 
-from . import ops
+from types import MethodType
+
+from . import _lib, ops
 from .gates import GateSpec, resolve
 
 
@@ -145,3 +156,128 @@ def install(model: torch.nn.Module, *, skip: bool = True) -> dict[str, Any]:
         layer.mlp = SparseGPTNeoXMLP.from_mlp(layer.mlp, skip=skip)
         gates.append(layer.mlp.gate.metadata())
     return {"mlp": "spmlp up_gate + down_sparse (sm_100a tcgen05)", "skip": skip, "gates": gates}
+
+
+def _branch_gate(module: Any, allowed: tuple[int, ...]) -> GateSpec | None:
+    """The reference joint's input gate for one branch, or None when it has none."""
+    if module is None:
+        return None
+    try:
+        spec = resolve(module)
+    except ValueError:
+        return None
+    return spec if spec.op in allowed else None
+
+
+class JointConsumer:
+    """The joint consumer of one parallel-residual GPT-NeoX layer, in one sm_100a kernel.
+
+    Mirrors the reference's ``Joint(layer)``: ``w2`` is ``layer.mlp.dense_4h_to_h``,
+    ``wo`` is ``layer.attention.dense``; ``gh`` / ``th`` come from ``layer.mlp.act``
+    (a one-sided threshold or ReLU) and ``gz`` / ``tz`` from ``layer.attention.z_gate``
+    (a one-sided threshold), as in runs/027-2026-09-06-pythia14m-kernel-sparsity-
+    characterization/adapter.py:37-41.  Output and gate buffers are owned by the
+    object and reused across calls.  Inference only, CUDA only, fp16 or bf16.
+    """
+
+    def __init__(self, layer: torch.nn.Module, *, skip: bool | str = True):
+        self.w2 = layer.mlp.dense_4h_to_h
+        self.wo = layer.attention.dense
+        self.h_gate = _branch_gate(getattr(layer.mlp, "act", None), (_lib.GATE_ONE_SIDED, _lib.GATE_RELU))
+        self.z_gate = _branch_gate(getattr(layer.attention, "z_gate", None), (_lib.GATE_ONE_SIDED,))
+        self.gh, self.gz = self.h_gate is not None, self.z_gate is not None
+        self.th = self.h_gate.kappa if self.gh else 0.0
+        self.tz = self.z_gate.kappa if self.gz else 0.0
+        self.skip = skip
+        self.stats: torch.Tensor | None = None
+        self._buffers: dict[str, torch.Tensor] = {}
+
+    def _buffer(self, name: str, shape: tuple[int, ...], like: torch.Tensor, dtype: torch.dtype | None = None):
+        dtype = dtype or like.dtype
+        buf = self._buffers.get(name)
+        if buf is None or buf.shape != shape or buf.dtype != dtype or buf.device != like.device:
+            buf = self._buffers[name] = torch.empty(shape, device=like.device, dtype=dtype)
+        return buf
+
+    def enable_stats(self) -> torch.Tensor:
+        """Start accumulating [issued, skipped] K16 MMA steps of the h branch."""
+        self.stats = torch.zeros(2, dtype=torch.int64, device=self.w2.weight.device)
+        return self.stats
+
+    def __call__(self, h: torch.Tensor, z: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """Reference contract: h is the ungated up-projection output, z the ungated
+        attention context; both gates are applied here."""
+        _inference_guard(h)
+        h2 = h.reshape(-1, h.shape[-1]).contiguous()
+        t, f = h2.shape
+        bits = self._buffer("bits", (ops.tile_bits_size(t, f),), h2, torch.int32)
+        if self.gh:
+            h2 = ops.gate(h2, self.h_gate, out=self._buffer("h", (t, f), h2), bits=bits)
+        else:
+            ops.tile_bits_from_h(h2, bits)
+        return self.forward_gated(h2, bits, z, residual)
+
+    def forward_gated(self, h: torch.Tensor, bits: torch.Tensor | None, z: torch.Tensor,
+                      residual: torch.Tensor) -> torch.Tensor:
+        """h already gated, with its tile bitmap (e.g. from ``ops.up_gate``)."""
+        _inference_guard(z)
+        z2 = z.reshape(-1, z.shape[-1]).contiguous()
+        r = residual.reshape(-1, residual.shape[-1]).contiguous()
+        if self.gz:
+            z2 = ops.gate(z2, self.z_gate, out=self._buffer("z", tuple(z2.shape), z2))
+        out = self._buffer("out", tuple(r.shape), r)
+        ops.joint(h, bits, z2, self.w2.weight, self.w2.bias, self.wo.weight, self.wo.bias, r, skip=self.skip,
+                  out=out, stats=self.stats)
+        return out.view_as(residual)
+
+
+def _joint_layer_forward(self, hidden_states, attention_mask=None, position_ids=None, use_cache=False,
+                         layer_past=None, position_embeddings=None, **kwargs):
+    """GPTNeoXLayer.forward with parallel residual, fused as in the reference's
+    layer_forward (k018 candidate.py:48-56): attention up to its context z, the
+    fused up projection + gate + bitmap, then the joint consumer."""
+    if use_cache or layer_past is not None or self.training:
+        raise ValueError("the joint consumer runs uncached inference only")
+    z, _ = self.attention(self.input_layernorm(hidden_states), attention_mask=attention_mask,
+                          position_ids=position_ids, layer_past=None, use_cache=False,
+                          position_embeddings=position_embeddings, **kwargs)
+    m = self.post_attention_layernorm(hidden_states)
+    joint = self._spmlp_joint
+    shape = m.shape
+    x = m.reshape(-1, shape[-1]).contiguous()
+    t, f = x.shape[0], joint.up.out_features
+    h = joint._buffer("h_up", (t, f), x)
+    bits = joint._buffer("bits_up", (ops.tile_bits_size(t, f),), x, torch.int32)
+    seq_len = shape[-2] if len(shape) >= 2 else t
+    ops.up_gate(x, joint.up.weight, joint.up.bias, joint.up_gate, h=h, bits=bits, seq_len=seq_len)
+    return joint.forward_gated(h, bits, z, hidden_states)
+
+
+def install_joint(model: torch.nn.Module, *, skip: bool | str = True) -> dict[str, Any]:
+    """Fuse every parallel-residual layer's output side into one joint kernel.
+
+    Per layer, as the reference's Adapter.install (k018 candidate.py:69-75): the
+    attention's dense projection becomes the joint's z branch (``attention.dense``
+    is replaced by Identity, so attention returns its context), the MLP's down
+    projection its h branch, and ``layer.forward`` calls up_gate then the joint.
+    The gate of h stays ``layer.mlp.act`` (applied by up_gate); a one-sided
+    ``attention.z_gate`` is applied to z by the joint and bypassed inside attention.
+    """
+    layers = getattr(getattr(model, "gpt_neox", None), "layers", None)
+    if layers is None:
+        raise ValueError("install_joint() needs a GPT-NeoX model (model.gpt_neox.layers)")
+    gates = []
+    for layer in layers:
+        if not getattr(layer, "use_parallel_residual", False):
+            raise ValueError("the joint consumer needs GPT-NeoX's parallel residual")
+        mlp = layer.mlp
+        joint = JointConsumer(layer, skip=skip)
+        joint.up = mlp.dense_h_to_4h
+        joint.up_gate = mlp.gate if isinstance(mlp, SparseGPTNeoXMLP) else resolve(getattr(mlp, "act", None))
+        layer._spmlp_joint = joint
+        layer.attention.dense = torch.nn.Identity()
+        if joint.gz:
+            layer.attention.z_gate.forward = MethodType(lambda self, x: x, layer.attention.z_gate)
+        layer.forward = MethodType(_joint_layer_forward, layer)
+        gates.append({"h": joint.up_gate.metadata(), "z": joint.z_gate.metadata() if joint.gz else None})
+    return {"joint": "spmlp up_gate + joint (sm_100a tcgen05)", "skip": skip, "gates": gates}

@@ -151,6 +151,73 @@ def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor,
     return y
 
 
+def joint(h: torch.Tensor, bits: torch.Tensor | None, z: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor | None,
+          wo: torch.Tensor, bo: torch.Tensor | None, residual: torch.Tensor | None = None, *,
+          skip: bool | str = True, out: torch.Tensor | None = None,
+          stats: torch.Tensor | None = None) -> torch.Tensor:
+    """out = round(round(round(h w2^T + b2) + round(z wo^T + bo)) + residual) in one kernel.
+
+    The joint consumer of a GPT-NeoX layer with parallel residual: h [T,F] (already
+    gated; bits its 16x64 tile bitmap), z [T,d] the attention context before its
+    output projection, w2 [d,F] / b2 [d] (dense_4h_to_h), wo [d,d] / bo [d]
+    (attention.dense), residual [T,d].  skip and stats as in ``down_sparse`` (the
+    z branch is dense).
+    """
+    device, dtype, code = _device_dtype(h)
+    t, f = h.shape
+    d = w2.shape[0]
+    _check("h", h, dtype, device)
+    _check("z", z, dtype, device, (t, d))
+    _check("w2", w2, dtype, device, (d, f))
+    _check("wo", wo, dtype, device, (d, d))
+    if b2 is not None:
+        _check("b2", b2, dtype, device, (d,))
+    if bo is not None:
+        _check("bo", bo, dtype, device, (d,))
+    if residual is not None:
+        _check("residual", residual, dtype, device, (t, d))
+    mode = _down_mode(skip)
+    if mode != _lib.DOWN_DENSE:
+        if bits is None:
+            raise ValueError("skipping needs the tile bitmap")
+        _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    if out is None:
+        out = torch.empty((t, d), device=device, dtype=dtype)
+    _check("out", out, dtype, device, (t, d))
+    if stats is not None:
+        _check("stats", stats, torch.int64, device, (2,))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_joint", _ptr(h), _ptr(bits) if mode != _lib.DOWN_DENSE else None, _ptr(z), _ptr(w2),
+                  _ptr(b2), _ptr(wo), _ptr(bo), _ptr(residual), _ptr(out), t, f, d, code, mode, _ptr(stats),
+                  _stream(device))
+    return out
+
+
+_ELEMENTWISE_GATES = (_lib.GATE_IDENTITY, _lib.GATE_ONE_SIDED, _lib.GATE_SYMMETRIC, _lib.GATE_RELU)
+
+
+def gate(x: torch.Tensor, gate, *, out: torch.Tensor | None = None,
+         bits: torch.Tensor | None = None) -> torch.Tensor:
+    """out = gate(x) for an elementwise gate (identity, one-sided, symmetric, ReLU);
+    ``out=x`` gates in place.  With ``bits`` (int32[tile_bits_size(T, F)]) the 16x64
+    tile bitmap of the result is written too."""
+    spec = resolve(gate)
+    if spec.op not in _ELEMENTWISE_GATES:
+        raise ValueError(f"spmlp gate takes an elementwise threshold gate or ReLU, not {spec.operator!r}")
+    device, dtype, code = _device_dtype(x)
+    t, f = x.shape
+    _check("x", x, dtype, device)
+    if out is None:
+        out = torch.empty_like(x)
+    _check("out", out, dtype, device, (t, f))
+    if bits is not None:
+        _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_gate", _ptr(x), _ptr(out), _ptr(bits), t, f, code, spec.op,
+                  ctypes.c_float(spec.kappa_for(dtype)), _stream(device))
+    return out
+
+
 def mlp_forward(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, w_out: torch.Tensor,
                 b_out: torch.Tensor | None, gate=None, *, residual: torch.Tensor | None = None, skip: bool | str = True,
                 h: torch.Tensor | None = None, bits: torch.Tensor | None = None, y: torch.Tensor | None = None,
@@ -255,6 +322,8 @@ _LIB = torch.library.Library("spmlp", "DEF")
 _LIB.define("up_gate(Tensor x, Tensor w_in, Tensor? b_in, int gate_op, float kappa, int seq_len) -> (Tensor, Tensor)")
 _LIB.define("down_sparse(Tensor h, Tensor? bits, Tensor w_out, Tensor? b_out, Tensor? residual, bool skip) -> Tensor")
 _LIB.define("head_sparse(Tensor x, Tensor w_vocab, Tensor? support, Tensor? active_tiles) -> Tensor")
+_LIB.define("joint(Tensor h, Tensor? bits, Tensor z, Tensor w2, Tensor? b2, Tensor wo, Tensor? bo, "
+            "Tensor? residual, bool skip) -> Tensor")
 
 _OP_NAMES = {v: k for k, v in OPERATORS.items()}
 
@@ -276,3 +345,10 @@ def _head_sparse_op(x, w_vocab, support, active_tiles):
 _LIB.impl("up_gate", _up_gate_op, "CUDA")
 _LIB.impl("down_sparse", _down_sparse_op, "CUDA")
 _LIB.impl("head_sparse", _head_sparse_op, "CUDA")
+
+
+def _joint_op(h, bits, z, w2, b2, wo, bo, residual, skip):
+    return joint(h, bits, z, w2, b2, wo, bo, residual, skip=bool(skip))
+
+
+_LIB.impl("joint", _joint_op, "CUDA")

@@ -62,6 +62,52 @@ def test_argument_errors_are_reported_without_a_gpu(lib):
     assert rc == -2  # corner gate: T=64 is not a multiple of seq_len=12
 
 
+def test_joint_and_gate_argument_errors_without_a_gpu(lib):
+    k = ctypes.c_float(0.5)
+    # h, bits, z, w2, b2, wo, bo, residual, out, T, F, d, dtype, mode, stats, stream
+    rc = lib.spmlp_joint(16, 16, 16, 16, None, 16, None, None, 16, 64, 512, 128, 0, 7, None, None)
+    assert rc == -1 and b"joint mode" in lib.spmlp_last_error()
+    rc = lib.spmlp_joint(16, None, 16, 16, None, 16, None, None, 16, 64, 512, 128, 0, 1, None, None)
+    assert rc == -1 and b"tile_bits" in lib.spmlp_last_error()
+    rc = lib.spmlp_joint(16, None, None, 16, None, 16, None, None, 16, 64, 512, 128, 0, 0, None, None)
+    assert rc == -1 and b"non-null" in lib.spmlp_last_error()
+    rc = lib.spmlp_joint(16, 16, 16, 16, None, 16, None, None, 16, 64, 512, 100, 0, 1, None, None)
+    assert rc == -2
+    rc = lib.spmlp_joint(17, 16, 16, 16, None, 16, None, None, 16, 64, 512, 128, 0, 1, None, None)
+    assert rc == -3
+    # x, out, bits, T, F, dtype, gate_op, kappa, stream
+    rc = lib.spmlp_gate(16, 16, None, 64, 512, 0, 1, k, None)
+    assert rc == -1 and b"gate" in lib.spmlp_last_error()  # GELU is not an elementwise threshold gate
+    rc = lib.spmlp_gate(16, 16, None, 64, 500, 0, 2, k, None)
+    assert rc == -2
+    rc = lib.spmlp_gate(16, 16, None, 64, 512, 0, 2, ctypes.c_float(-1.0), None)
+    assert rc == -1 and b"kappa" in lib.spmlp_last_error()
+    rc = lib.spmlp_gate(16, 1024, None, 64, 512, 0, 2, k, None)
+    assert rc == -1 and b"overlap" in lib.spmlp_last_error()
+
+
+def test_joint_consumer_reads_the_reference_gates():
+    from types import SimpleNamespace
+
+    from sparsity_spillover_b200 import JointConsumer
+
+    lin2, lino = torch.nn.Linear(512, 128), torch.nn.Linear(128, 128)
+    layer = SimpleNamespace(mlp=SimpleNamespace(dense_4h_to_h=lin2, act=FixedOneSidedThreshold(0.25)),
+                            attention=SimpleNamespace(dense=lino, z_gate=FixedOneSidedThreshold(0.5)))
+    j = JointConsumer(layer)
+    assert (j.gh, j.gz, j.th, j.tz) == (True, True, 0.25, 0.5) and j.w2 is lin2 and j.wo is lino
+    relu = SimpleNamespace(mlp=SimpleNamespace(dense_4h_to_h=lin2, act=torch.nn.ReLU()),
+                           attention=SimpleNamespace(dense=lino))
+    j = JointConsumer(relu)
+    assert (j.gh, j.gz, j.th) == (True, False, 0.0)
+    gelu = SimpleNamespace(mlp=SimpleNamespace(dense_4h_to_h=lin2, act=None),
+                           attention=SimpleNamespace(dense=lino, z_gate=FixedSymmetricThreshold(0.1)))
+    j = JointConsumer(gelu)
+    assert (j.gh, j.gz) == (False, False)  # the reference joint gates only with one-sided z gates
+    with pytest.raises(ValueError):
+        j(torch.zeros(64, 512), torch.zeros(64, 128), torch.zeros(64, 128))  # CPU tensors: no fallback
+
+
 def test_ops_refuse_cpu_tensors():
     from sparsity_spillover_b200 import ops
 
