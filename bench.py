@@ -331,6 +331,55 @@ def head_bench(device, steps=5) -> list[dict]:
     return rows
 
 
+def joint_cfg1(device, steps: int = 10) -> dict:
+    """The joint consumer on the cfg1 layer shape (T=32768, d=512, F=2048, fp16; h from
+    up_gate at 10 % element density, attention context z ~ N(0,1), residual x):
+    out = round(round(round(h W2^T + b2) + round(z Wo^T + bo)) + x) as one kernel,
+    against our down projection followed by PyTorch's output projection and adds,
+    and against stock PyTorch for all of it; each captured as a CUDA graph."""
+    import torch
+    import torch.nn.functional as fn
+
+    from sparsity_spillover_b200 import ops, workloads
+
+    cfg = workloads.CONFIGS["cfg1"]
+    layer = workloads.make_weights(cfg, device)[0]
+    x = workloads.make_input(cfg, device)
+    t, d, f = x.shape[0], cfg.d, cfg.F
+    zc = torch.empty(t, f, dtype=cfg.dtype, device=device)
+    ops.up_gate(x, layer.w_in, layer.b_in, {"operator": "identity"}, z_out=zc)
+    gate = {"operator": "one_sided_threshold", "kappa": workloads.quantile_threshold(zc, DENSITY)}
+    del zc
+    h, bits = ops.up_gate(x, layer.w_in, layer.b_in, gate)
+    g = torch.Generator(device=device).manual_seed(77)
+    z = torch.randn(t, d, generator=g, device=device).to(cfg.dtype)
+    wo = (torch.randn(d, d, generator=g, device=device) * 0.02).to(cfg.dtype)
+    bo = (torch.randn(d, generator=g, device=device) * 0.02).to(cfg.dtype)
+    out, y, out_split = (torch.empty(t, d, dtype=cfg.dtype, device=device) for _ in range(3))
+
+    def fused():
+        ops.joint(h, bits, z, layer.w_out, layer.b_out, wo, bo, x, out=out)
+
+    def split():
+        ops.down_sparse(h, bits, layer.w_out, layer.b_out, y=y)
+        torch.add(torch.add(y, fn.linear(z, wo, bo)), x, out=out_split)
+
+    def stock():
+        return torch.add(torch.add(fn.linear(h, layer.w_out, layer.b_out), fn.linear(z, wo, bo)), x)
+
+    times = {name: time_device(graph_of(f_, device).replay, steps, device)
+             for name, f_ in (("fused", fused), ("split", split), ("stock", stock))}
+    ref = stock()
+    torch.cuda.synchronize(device)
+    err = float((out.double() - ref.double()).abs().max() / ref.double().abs().max())
+    flop = 2.0 * t * f * d + 2.0 * t * d * d
+    tflops = flop / times["fused"] / 1e12
+    return {"tokens": t, "d": d, "F": f, "density": DENSITY, "fused_us": times["fused"] * 1e6,
+            "down_sparse_plus_torch_us": times["split"] * 1e6, "stock_pytorch_us": times["stock"] * 1e6,
+            "speedup_vs_split": times["split"] / times["fused"], "speedup_vs_stock": times["stock"] / times["fused"],
+            "executed_tflops": tflops, "max_rel_diff_vs_stock_pytorch": err}
+
+
 def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int = 3) -> dict:
     """410M shape, `layers` layers: d_ff split over the ranks (reduce-scatter + all-gather per
     layer over NCCL) against token sharding of the same per-rank token count (no collective)."""
@@ -579,6 +628,7 @@ def run_ours(args):
             line["tile_structured_cfg2"] = tile_structured(device)
             line["pythia410m_cfg3"] = cfg3_410m(device)
             line["vocab_head_cfg4"] = head_bench(device)
+            line["joint_cfg1"] = joint_cfg1(device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
     if world > 1:

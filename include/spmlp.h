@@ -125,7 +125,7 @@ int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_ou
  *   and runs/042-2026-09-20-pythia70m-sparse-scale/controls.py:19-26.
  *   The reference's input gates (h < th and z < tz set to zero) are applied
  *   beforehand with spmlp_gate.  mode and stats as spmlp_down_sparse (over the
- *   h branch; z is dense); output tiles are spmlp_down_tile_tokens(mode) x 128. */
+ *   h branch; z is dense); output tiles are spmlp_down_tile_tokens(mode) x 256. */
 int spmlp_joint(const void* h, const uint32_t* tile_bits, const void* z, const void* w2, const void* b2,
                 const void* wo, const void* bo, const void* residual, void* out, int64_t T, int F, int d,
                 int dtype, int mode, uint64_t* stats, void* stream);

@@ -6,8 +6,8 @@
 //               into a STAGES-deep shared-memory ring, so the ring holds the
 //               surviving tiles back to back (compaction through smem).
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128,
-//               or M=256 over a CTA pair, N=BN, K=16) into a double-buffered
-//               TMEM accumulator.
+//               or M=256 over a CTA pair, N=BN, K=16) into TMEM accumulators,
+//               double-buffered across tiles when two tiles' worth fit.
 //   warps 2..   epilogue (4 or 8 warps): tcgen05.ld the accumulator (one
 //               token row per thread, software-pipelined), apply the
 //               kind-specific epilogue, stage 32x32 chunks in shared memory
@@ -162,7 +162,10 @@ struct GemmTraits {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr int kAccs = KIND == KIND_JOINT ? 2 : 1;     // accumulators per tile
   static constexpr uint32_t kAccCols = kAccs * BN;               // TMEM columns of one tile's accumulators
-  static constexpr uint32_t kTmemCols = 2 * kAccCols;  // double-buffered (this CTA's M half)
+  // Double-buffered when two tiles' accumulators fit in TMEM's 512 columns (this
+  // CTA's M half); a joint tile of BN = 256 fills TMEM alone and is single-buffered.
+  static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr uint32_t kTmemCols = kAccBufs * kAccCols;
   static constexpr int kEpiWarps = EPI;          // 4: one warp per TMEM lane quarter; 8: two, splitting columns
   static constexpr int kThreads = 64 + 32 * EPI;
   static constexpr uint32_t kStageOutBytes = 32 * 32 * 2;  // one 32-row x 32-column output chunk
@@ -569,7 +572,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         if (!ok) break;
         if (lane == 0) umma_commit<CG>(&acc_full[acc]);
         __syncwarp();
-        if (++acc == 2) {
+        if (++acc == Tr::kAccBufs) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -863,7 +866,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           }
         }
       }
-      if (has_acc && ++acc == 2) {
+      if (has_acc && ++acc == Tr::kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;
       }

@@ -52,9 +52,12 @@ constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
 constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
 constexpr int kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
-// Joint consumer: 128 output columns per tile so that both accumulators of a
-// tile fit twice in TMEM (2 x 2 x 128 columns); 24 KB (pair) / 32 KB stages.
-constexpr int kJointBN = 128, kJointStages = 8, kJointFineStages = 6, kJointEpiWarps = 4, kJointRing = 2;
+// Joint consumer: 256 output columns per tile, so that h is read by only d/256
+// column tiles; the tile's two accumulators then fill TMEM's 512 columns and are
+// single-buffered (measured on cfg1: 96 us against 121 us for double-buffered
+// 128-column tiles, which read h twice as often).
+constexpr int kJointBN = 256, kJointStages = 5, kJointEpiWarps = 8, kJointRing = 2;
+constexpr int kJointFineStages = 4, kJointFineEpiWarps = 4;
 
 struct DeviceInfo {
   int sm_count = 0;
@@ -369,14 +372,14 @@ int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w
   p.bits_words = spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  constexpr int E = kJointEpiWarps, R = kJointRing;
+  constexpr int R = kJointRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
   if (mode == SPMLP_DOWN_SKIP_FINE) {
-    constexpr int S = kJointFineStages;
+    constexpr int S = kJointFineStages, E = kJointFineEpiWarps;
     if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
     return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
   }
-  constexpr int S = kJointStages;
+  constexpr int S = kJointStages, E = kJointEpiWarps;
   if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
   return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
 }

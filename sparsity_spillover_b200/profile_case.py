@@ -3,12 +3,15 @@
     python -m sparsity_spillover_b200.profile_case --case mlp  [--tokens 32768] [--iters 3]
     python -m sparsity_spillover_b200.profile_case --case tile [--p 0.1]
     python -m sparsity_spillover_b200.profile_case --case head [--d 128] [--frac 0.1]
+    python -m sparsity_spillover_b200.profile_case --case joint [--tokens 32768]
 
 * ``mlp``  one cfg1 layer (d=512, F=2048, fp16, one-sided gate at 10% density):
            up_gate then down_sparse with the residual, ``iters`` times.
 * ``tile`` cfg2: a tile-structured bf16 h (64x64 tiles live with probability p),
            its bitmap, and the tile-skipping down_sparse (d=512, F=2048).
 * ``head`` cfg4: the N-gated vocabulary head on Zipf-chosen 128-column tiles.
+* ``joint`` the joint consumer on a cfg1 layer: up_gate (identity, then gated) once,
+           then the joint kernel ``iters`` times (h at 10% density, z ~ N(0,1)).
 
 Inputs are seeded synthetic tensors; device memory stays well under 1 GB.
 """
@@ -23,7 +26,7 @@ from . import ops, workloads
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--case", choices=["mlp", "tile", "head"], default="mlp")
+    ap.add_argument("--case", choices=["mlp", "tile", "head", "joint"], default="mlp")
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--p", type=float, default=0.1)
@@ -32,7 +35,7 @@ def main() -> None:
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     with torch.inference_mode():
-        if args.case == "mlp":
+        if args.case in ("mlp", "joint"):
             cfg = workloads.CONFIGS["cfg1"]
             layer = workloads.make_weights(cfg, dev)[0]
             x = workloads.make_input(cfg, dev, tokens=args.tokens)
@@ -43,7 +46,16 @@ def main() -> None:
             h = torch.empty(args.tokens, cfg.F, dtype=cfg.dtype, device=dev)
             bits = torch.empty(ops.tile_bits_size(args.tokens, cfg.F), dtype=torch.int32, device=dev)
             y = torch.empty_like(x)
+            if args.case == "joint":
+                ops.up_gate(x, layer.w_in, layer.b_in, gate, h=h, bits=bits)
+                g = torch.Generator(device=dev).manual_seed(77)
+                z = torch.randn(args.tokens, cfg.d, generator=g, device=dev).to(cfg.dtype)
+                wo = (torch.randn(cfg.d, cfg.d, generator=g, device=dev) * 0.02).to(cfg.dtype)
+                bo = (torch.randn(cfg.d, generator=g, device=dev) * 0.02).to(cfg.dtype)
             for _ in range(args.iters):
+                if args.case == "joint":
+                    ops.joint(h, bits, z, layer.w_out, layer.b_out, wo, bo, x, out=y)
+                    continue
                 ops.up_gate(x, layer.w_in, layer.b_in, gate, h=h, bits=bits)
                 ops.down_sparse(h, bits, layer.w_out, layer.b_out, x, y=y)
         elif args.case == "tile":

@@ -128,7 +128,7 @@ def test_joint_skips_dead_tiles_of_h_and_counts_them(skip):
     ref = omlp.joint(h, z, w2, b2, wo, bo, r, 0.0, 0.0, False, False)
     assert omlp.max_rel_error(out.cpu(), ref) <= TOL[dtype]
     mask = obit.tile_mask(h.float(), 16, 64)
-    issued, skipped = obit.skip_counts(mask, f, n_tiles=d // 128, m_tile=ops.down_tile_tokens(skip))
+    issued, skipped = obit.skip_counts(mask, f, n_tiles=d // 256, m_tile=ops.down_tile_tokens(skip))
     assert stats.cpu().tolist() == [issued, skipped]
     assert skipped > 0
 
