@@ -381,8 +381,9 @@ def joint_cfg1(device, steps: int = 10) -> dict:
 
 
 def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int = 3) -> dict:
-    """410M shape, `layers` layers: d_ff split over the ranks (reduce-scatter + all-gather per
-    layer over NCCL) against token sharding of the same per-rank token count (no collective)."""
+    """410M shape, `layers` layers: d_ff split over the ranks, with the reduce-scatter and the
+    next layer's all-gather either as NCCL collectives or fused into the kernels (P2P over
+    NVLink), against token sharding of the same per-rank token count (no collective)."""
     import torch
     import torch.distributed as dist
 
@@ -411,8 +412,13 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
                                   y=bufs[i % 2])
         return cur
 
+    fused = sdist.FusedDffSplit(split, t_rank * world)
+
+    def run_fused():
+        return fused.forward(x_all)
+
     out = {}
-    for name, fn in (("dff_split", run_split), ("token_sharded", run_tokens)):
+    for name, fn in (("dff_split", run_split), ("dff_split_fused", run_fused), ("token_sharded", run_tokens)):
         fn()
         dist.barrier(device_ids=[device.index])
         t = max_over_ranks(time_device(fn, steps, device), world, device)

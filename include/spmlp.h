@@ -109,6 +109,26 @@ int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_ou
                       const void* residual, void* y, int64_t T, int F, int d, int dtype, int mode,
                       uint64_t* stats, void* stream);
 
+/* d_ff split with the reduce-scatter fused into the down projection.  No
+ * counterpart in the reference (it runs on one GPU); it replaces the partial
+ * down projection followed by an NCCL reduce-scatter (ncclReduceScatter of the
+ * partial y over tokens) that a d_ff split of GPTNeoXMLP.dense_4h_to_h needs.
+ *   spmlp_down_scatter: as spmlp_down_sparse without bias and residual, but the
+ *   rounded partial of tokens [j*T/world, (j+1)*T/world) is stored into
+ *   slots[j] ([T/world, d], this rank's slot in rank j's receive buffer, peer
+ *   memory reachable over NVLink) while the other tiles are still computing.
+ *   T/world must be a multiple of 256.
+ *   spmlp_reduce_broadcast: after every rank's scatter has completed (the caller
+ *   orders it, e.g. with a one-element all-reduce), for this rank's token block:
+ *   y = round(round(sum_r recv[r] + b_out) + residual), the sum in fp32 in rank
+ *   order, written to each of targets[0..n_targets) (this rank's block of each
+ *   rank's copy of the next layer's input: the all-gather of the next input in
+ *   the same pass).  recv [world, rows, d]; residual may be one of the targets. */
+int spmlp_down_scatter(const void* h, const uint32_t* tile_bits, const void* w_out, void* const* slots, int world,
+                       int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, void* stream);
+int spmlp_reduce_broadcast(const void* recv, int world, int64_t rows, int d, const void* b_out,
+                           const void* residual, void* const* targets, int n_targets, int dtype, void* stream);
+
 /* Joint consumer: the MLP's down projection and the attention output
  * projection of one GPT-NeoX layer, summed with its parallel residual, in one
  * kernel.  Replaces the reference's joint (the k018 Joint.__call__ of

@@ -25,6 +25,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_tile_bits_from_h": (I32, [VP, VP, I64, I32, I32, VP]),
     "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
     "spmlp_down_sparse": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
+    "spmlp_down_scatter": (I32, [VP, VP, VP, _c.POINTER(VP), I32, I64, I32, I32, I32, I32, VP, VP]),
+    "spmlp_reduce_broadcast": (I32, [VP, I32, I64, I32, VP, VP, _c.POINTER(VP), I32, I32, VP]),
     "spmlp_joint": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_gate": (I32, [VP, VP, VP, I64, I32, I32, I32, F32, VP]),
     "spmlp_mlp_forward": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, I32, VP, VP]),

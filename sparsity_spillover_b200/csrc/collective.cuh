@@ -1,0 +1,60 @@
+// Reduction side of the d_ff split's fused reduce-scatter.
+//
+// Each rank's scattering down projection (GemmParams::scatter_rows) has written
+// its rounded partial of this rank's token block into slot r of this rank's
+// receive buffer recv [world, rows, d].  This kernel finishes the layer for the
+// block: y = round(round(sum_r recv[r] + b_out) + residual), the sum in fp32 in
+// rank order (deterministic), and writes y to every target -- each rank's copy
+// of the next layer's input, so the reduction and the all-gather of the next
+// input are one pass over NVLink.
+#pragma once
+
+#include <stdint.h>
+
+#include "gemm_sm100.cuh"
+
+namespace spmlp {
+
+struct BroadcastTargets {
+  void* dst[kMaxRanks];  // this rank's token block inside each target buffer
+  int n;
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) reduce_broadcast_kernel(const uint16_t* __restrict__ recv, int world,
+                                                               int64_t elems, int d, const uint16_t* __restrict__ bias,
+                                                               const uint16_t* residual, BroadcastTargets targets) {
+  using D = DType<BF16>;
+  const int64_t vecs = elems / 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < world; ++r) {
+      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(recv + r * elems) + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] += D::lo(w[j]);
+        acc[2 * j + 1] += D::hi(w[j]);
+      }
+    }
+    uint32_t out[4];
+    const int col = static_cast<int>((i * 8) % d);
+    uint4 b = make_uint4(0u, 0u, 0u, 0u);
+    if (bias != nullptr) b = __ldg(reinterpret_cast<const uint4*>(bias + col));
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(acc[2 * j] + D::lo(bw[j]), acc[2 * j + 1] + D::hi(bw[j]));
+    if (residual != nullptr) {
+      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(rw[j]), D::hi(out[j]) + D::hi(rw[j]));
+    }
+    const uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
+    for (int k = 0; k < targets.n; ++k) reinterpret_cast<uint4*>(targets.dst[k])[i] = o;
+  }
+  __threadfence_system();  // peer stores are performed before the kernel completes
+}
+
+}  // namespace spmlp

@@ -52,6 +52,7 @@ constexpr int kBM = 128;       // tokens per tile (UMMA M)
 constexpr int kBK = 64;        // K elements per pipeline stage (one 128-byte swizzle row)
 constexpr int kBitsRows = 16;  // bitmap tile height (tokens)
 constexpr int kBitsCols = 64;  // bitmap tile width (features)
+constexpr int kMaxRanks = 8;   // ranks a scattering down projection can address
 
 struct GemmParams {
   int M, N, K;            // tokens, output columns, reduction length
@@ -71,6 +72,12 @@ struct GemmParams {
   float kappa;            // already rounded to the activation dtype
   int seq_len;            // GATE_CORNER: tokens per sequence (blocks restart per sequence)
   unsigned long long* stats;  // nullable: [0] issued K granules, [1] skipped K granules
+  // KIND_DOWN, d_ff split: with scatter_rows > 0 the rounded partial tile of tokens
+  // [j * scatter_rows, (j + 1) * scatter_rows) goes to scatter_out[j] (this rank's
+  // slot in rank j's receive buffer, [scatter_rows, N], usually peer memory)
+  // instead of `out`; bias and residual are added after the reduction.
+  void* scatter_out[kMaxRanks];
+  int scatter_rows;
   int* status;            // device status word
 };
 
@@ -606,6 +613,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     float* bias2_s = bias_s + EPI * kMyChunks * 32;  // KIND_JOINT: the second product's bias
     constexpr bool kHasRes = KIND == KIND_DOWN || KIND == KIND_JOINT;
     const bool with_res = kHasRes && p.residual != nullptr;
+    const bool scatter = KIND == KIND_DOWN && p.scatter_rows > 0;
     int ring_slot = 0;  // RING > 0: next slot of this warp's ring (carries across tiles)
     // The accumulator-release barriers live in the leader CTA.
     uint32_t acc_empty_addr[2];
@@ -773,12 +781,25 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
             if (ball & 0x0000ffffu) nz_bits |= 1u << (2 * grp);
             if (ball & 0xffff0000u) nz_bits |= 1u << (2 * grp + 1);
           }
-          // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) in this warp's tile slab.
+          if (scatter) {
+            // The partial chunk goes straight to its token block's owner (peer memory over NVLink).
+            if (row_ok) {
+              const int owner = row / p.scatter_rows;
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.scatter_out[owner]) +
+                                                    static_cast<size_t>(row - owner * p.scatter_rows) * p.N + col0);
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
-                make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+              for (int c = 0; c < 4; ++c)
+                dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+            }
+          } else {
+            // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) in this warp's tile slab.
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
+                  make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+          }
         }
+        if (scatter) return;  // nothing staged for a TMA store
         if constexpr (kRing) {
           // One fence and one TMA store per chunk; the slot is reused RING chunks later.
           fence_proxy_async_smem();
@@ -871,6 +892,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         acc_phase ^= 1u;
       }
     }
+    if (scatter) __threadfence_system();  // peer stores are performed before the kernel completes
     if (lane == 0) bulk_wait_group<0>();  // stores complete before the CTA's shared memory goes away
     __syncwarp();
   }

@@ -14,6 +14,7 @@
 #include "gemm_sm100.cuh"
 #include "head_prepare.cuh"
 #include "bitmap.cuh"
+#include "collective.cuh"
 #include "spmlp.h"
 
 namespace spmlp {
@@ -285,9 +286,21 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   return launch_up<BN>(ta, tb, tc, p, gate_op, bf16, stream, dev);
 }
 
+// slots != nullptr: the d_ff split's scattering mode (see GemmParams::scatter_out);
+// y is then unused and bias and residual must be null.
 int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void* b_out, const void* residual, void* y,
-              int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, cudaStream_t stream) {
+              int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, cudaStream_t stream,
+              void* const* slots = nullptr, int world = 0) {
   int rc;
+  if (slots != nullptr) {
+    if (world < 1 || world > kMaxRanks) return fail(SPMLP_EINVAL, "world=%d must be in [1, %d]", world, kMaxRanks);
+    if (T % world) return fail(SPMLP_ESHAPE, "T=%lld must divide evenly over %d ranks", (long long)T, world);
+    if ((T / world) % (kBM * kDownCG))
+      return fail(SPMLP_ESHAPE, "tokens per rank (%lld) must be a multiple of %d", (long long)(T / world), kBM * kDownCG);
+    for (int j = 0; j < world; ++j)
+      if (!slots[j] || !aligned16(slots[j])) return fail(SPMLP_EALIGN, "receive slot %d must be non-null and 16-byte aligned", j);
+    y = slots[0];  // the output map is encoded but not stored through in this mode
+  }
   if (!h || !w_out || !y) return fail(SPMLP_EINVAL, "h, w_out and y must be non-null");
   if (mode != SPMLP_DOWN_DENSE && mode != SPMLP_DOWN_SKIP && mode != SPMLP_DOWN_SKIP_FINE)
     return fail(SPMLP_EINVAL, "unknown down mode %d", mode);
@@ -321,6 +334,10 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   p.bits_words = spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
+  if (slots != nullptr) {
+    p.scatter_rows = static_cast<int>(T / world);
+    for (int j = 0; j < world; ++j) p.scatter_out[j] = slots[j];
+  }
   constexpr int S = kDownStages, E = kDownEpiWarps, C = kDownCG, R = kDownRing;
   constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps, RF = kDownFineRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
@@ -382,6 +399,41 @@ int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w
   constexpr int S = kJointStages, E = kJointEpiWarps;
   if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
   return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+}
+
+int reduce_broadcast_impl(const void* recv, int world, int64_t rows, int d, const void* b_out, const void* residual,
+                          void* const* targets, int n_targets, int dtype, cudaStream_t stream) {
+  int rc;
+  if (!recv || !targets) return fail(SPMLP_EINVAL, "recv and targets must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (world < 1 || world > kMaxRanks) return fail(SPMLP_EINVAL, "world=%d must be in [1, %d]", world, kMaxRanks);
+  if (n_targets < 1 || n_targets > kMaxRanks)
+    return fail(SPMLP_EINVAL, "n_targets=%d must be in [1, %d]", n_targets, kMaxRanks);
+  if (rows < 1 || rows >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "rows must be in [1, 2^31)");
+  if (d < kBitsCols || d % kBitsCols) return fail(SPMLP_ESHAPE, "d=%d must be a positive multiple of 64", d);
+  if (!aligned16(recv) || (b_out && !aligned16(b_out)) || (residual && !aligned16(residual)))
+    return fail(SPMLP_EALIGN, "recv, b_out and residual must be 16-byte aligned");
+  BroadcastTargets tg{};
+  tg.n = n_targets;
+  for (int k = 0; k < n_targets; ++k) {
+    if (!targets[k] || !aligned16(targets[k])) return fail(SPMLP_EALIGN, "target %d must be non-null and 16-byte aligned", k);
+    tg.dst[k] = targets[k];
+  }
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int64_t elems = rows * d;
+  const int64_t vecs = elems / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(dev->sm_count) * 8));
+  const uint16_t* rv = static_cast<const uint16_t*>(recv);
+  const uint16_t* bv = static_cast<const uint16_t*>(b_out);
+  const uint16_t* resv = static_cast<const uint16_t*>(residual);
+  if (dtype == SPMLP_BF16)
+    reduce_broadcast_kernel<true><<<blocks, 256, 0, stream>>>(rv, world, elems, d, bv, resv, tg);
+  else
+    reduce_broadcast_kernel<false><<<blocks, 256, 0, stream>>>(rv, world, elems, d, bv, resv, tg);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "reduce_broadcast_kernel launch");
+  return 0;
 }
 
 int gate_impl(const void* x, void* out, uint32_t* bits, int64_t T, int F, int dtype, int gate_op, float kappa,
@@ -622,6 +674,19 @@ int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_ou
                       void* stream) {
   return down_impl(h, tile_bits, w_out, b_out, residual, y, T, F, d, dtype, mode, stats,
                    static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_down_scatter(const void* h, const uint32_t* tile_bits, const void* w_out, void* const* slots, int world,
+                       int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, void* stream) {
+  if (!slots) return fail(SPMLP_EINVAL, "slots must be non-null");
+  return down_impl(h, tile_bits, w_out, nullptr, nullptr, nullptr, T, F, d, dtype, mode, stats,
+                   static_cast<cudaStream_t>(stream), slots, world);
+}
+
+int spmlp_reduce_broadcast(const void* recv, int world, int64_t rows, int d, const void* b_out, const void* residual,
+                           void* const* targets, int n_targets, int dtype, void* stream) {
+  return reduce_broadcast_impl(recv, world, rows, d, b_out, residual, targets, n_targets, dtype,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int spmlp_joint(const void* h, const uint32_t* tile_bits, const void* z, const void* w2, const void* b2,

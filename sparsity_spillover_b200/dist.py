@@ -10,9 +10,14 @@ Two partitions:
   with ``F_r = [r F / w, (r + 1) F / w)``.  Every rank runs the fused up-projection +
   gate + bitmap and the tile-skipping down-projection on its slice for the same
   token block, producing a partial ``Y_r [T, d]``; a reduce-scatter over the token
-  dimension (NCCL over NVLink on B200) sums the partials, and ``b_out`` (and the
-  residual) are added once after the sum.  The bitmap stays rank-local: each slice's
-  tiles are exactly the columns of the full bitmap for that slice.
+  dimension sums the partials, and ``b_out`` (and the residual) are added once after
+  the sum.  The bitmap stays rank-local: each slice's tiles are exactly the columns
+  of the full bitmap for that slice.  ``DffSplitMLP`` / ``dff_split_forward`` do the
+  reduce-scatter and the next layer's all-gather with NCCL; ``FusedDffSplit`` fuses
+  them into the kernels: the down projection stores each partial tile straight into
+  its owner's receive buffer over NVLink (peer memory from torch's symmetric memory)
+  while later tiles still compute, and one reduction kernel per rank sums its block
+  and writes the result into every rank's copy of the next layer's input.
 
 The reference has no distributed code; this module is new.  The compute callable
 is injectable (as the reference's adapters inject a PyTorch ``backend`` for tests,
@@ -144,3 +149,76 @@ def dff_split_forward(layers: list[DffSplitMLP], x: torch.Tensor) -> torch.Tenso
         if i + 1 < len(layers):
             cur = all_gather_tokens(shard, world, layer.group)
     return shard
+
+
+class FusedDffSplit:
+    """A stack of d_ff-split layers with the reduce-scatter and all-gather fused into
+    the kernels (``spmlp_down_scatter`` / ``spmlp_reduce_broadcast``) over NVLink.
+
+    Per layer: up_gate on the replicated input X (local); the scattering down
+    projection writes rank r's partial of token block j into slot r of rank j's
+    receive buffer; a one-element all-reduce orders it before every rank's
+    reduction, which sums its block's slots in fp32, adds b_out and the residual
+    (rounding like ``DffSplitMLP.forward``) and writes the block into every rank's X;
+    a second one-element all-reduce orders that before the next layer.  X and the
+    receive buffers are torch symmetric-memory tensors, so peers' addresses come
+    from its rendezvous; tokens per rank must be a multiple of 256.
+    """
+
+    def __init__(self, layers: list[DffSplitMLP], tokens: int, *, skip: bool | str = True):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import ops
+
+        if not layers:
+            raise ValueError("need at least one layer")
+        self.layers = layers
+        self.group = layers[0].group
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if tokens % self.world or (tokens // self.world) % 256:
+            raise ValueError(f"T={tokens} must split into {self.world} token blocks of a multiple of 256")
+        w = layers[0].w_in
+        self.device, self.dtype = w.device, w.dtype
+        self.d, self.f = w.shape[1], w.shape[0]
+        self.tokens, self.rows = tokens, tokens // self.world
+        self.skip = skip
+        group = self.group or dist.group.WORLD
+        if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(
+                group.group_name):
+            symm_mem.enable_symm_mem_for_group(group.group_name)
+        self.x = symm_mem.empty((tokens, self.d), dtype=self.dtype, device=self.device)
+        self.recv = symm_mem.empty((self.world, self.rows, self.d), dtype=self.dtype, device=self.device)
+        hx = symm_mem.rendezvous(self.x, group)
+        hr = symm_mem.rendezvous(self.recv, group)
+        esize = self.x.element_size()
+        block = self.rows * self.d * esize
+        # My slot in each rank's receive buffer, and my token block in each rank's X.
+        self.slots = [int(hr.buffer_ptrs[j]) + self.rank * block for j in range(self.world)]
+        self.targets = [int(hx.buffer_ptrs[j]) + self.rank * block for j in range(self.world)]
+        self._handles = (hx, hr)
+        self.h = torch.empty((tokens, self.f), dtype=self.dtype, device=self.device)
+        self.bits = torch.empty((ops.tile_bits_size(tokens, self.f),), dtype=torch.int32, device=self.device)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def _barrier(self) -> None:
+        dist.all_reduce(self._flag, group=self.group)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x [T, d] (the same on every rank) -> this rank's [T/w, d] block of the last
+        layer's output; the whole output is in ``self.x`` on every rank."""
+        from . import ops
+
+        if tuple(x.shape) != (self.tokens, self.d):
+            raise ValueError(f"x must be [{self.tokens}, {self.d}]")
+        # The previous call ended with a barrier after every rank's last broadcast, so
+        # overwriting X here races with no other rank.
+        self.x.copy_(x)
+        mine = self.x[self.rank * self.rows:(self.rank + 1) * self.rows]
+        for layer in self.layers:
+            ops.up_gate(self.x, layer.w_in, layer.b_in, layer.gate, h=self.h, bits=self.bits)
+            ops.down_scatter(self.h, self.bits, layer.w_out, self.slots, skip=self.skip)
+            self._barrier()
+            ops.reduce_broadcast(self.recv, layer.b_out, mine, self.targets)
+            self._barrier()
+        return mine

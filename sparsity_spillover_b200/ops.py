@@ -151,6 +151,53 @@ def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor,
     return y
 
 
+def _pointer_array(ptrs: list[int]):
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    return ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)), arr
+
+
+def down_scatter(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor, slots: list[int], *,
+                 skip: bool | str = True, stats: torch.Tensor | None = None) -> None:
+    """Partial down projection of a d_ff slice, scattered by token block: the rounded
+    partial of tokens [j T/w, (j+1) T/w) is stored at device address ``slots[j]``
+    (this rank's slot in rank j's receive buffer, typically peer memory)."""
+    device, dtype, code = _device_dtype(h)
+    t, f = h.shape
+    d = w_out.shape[0]
+    _check("h", h, dtype, device)
+    _check("w_out", w_out, dtype, device, (d, f))
+    mode = _down_mode(skip)
+    if mode != _lib.DOWN_DENSE:
+        if bits is None:
+            raise ValueError("skipping needs the tile bitmap")
+        _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    if stats is not None:
+        _check("stats", stats, torch.int64, device, (2,))
+    arr, keep = _pointer_array([int(v) for v in slots])
+    with torch.cuda.device(device):
+        _lib.call("spmlp_down_scatter", _ptr(h), _ptr(bits) if mode != _lib.DOWN_DENSE else None, _ptr(w_out), arr,
+                  len(slots), t, f, d, code, mode, _ptr(stats), _stream(device))
+    del keep
+
+
+def reduce_broadcast(recv: torch.Tensor, b_out: torch.Tensor | None, residual: torch.Tensor | None,
+                     targets: list[int]) -> None:
+    """y = round(round(sum_r recv[r] + b_out) + residual) for recv [world, rows, d],
+    written to each device address in ``targets`` (rows x d each)."""
+    device, dtype, code = _device_dtype(recv)
+    world, rows, d = recv.shape
+    _check("recv", recv, dtype, device)
+    if b_out is not None:
+        _check("b_out", b_out, dtype, device, (d,))
+    if residual is not None:
+        _check("residual", residual, dtype, device, (rows, d))
+    arr, keep = _pointer_array([int(v) for v in targets])
+    with torch.cuda.device(device):
+        _lib.call("spmlp_reduce_broadcast", _ptr(recv), world, rows, d, _ptr(b_out), _ptr(residual), arr, len(targets),
+                  code, _stream(device))
+    del keep
+
+
 def joint(h: torch.Tensor, bits: torch.Tensor | None, z: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor | None,
           wo: torch.Tensor, bo: torch.Tensor | None, residual: torch.Tensor | None = None, *,
           skip: bool | str = True, out: torch.Tensor | None = None,

@@ -1,6 +1,8 @@
 """Two-GPU checks (skipped with fewer GPUs): the d_ff split with an NCCL
-reduce-scatter over NVLink matches one GPU within tolerance, and token shards
-are bit-identical to the single-GPU forward of the same tokens."""
+reduce-scatter over NVLink, and the fused d_ff split (partials stored into the
+owner's buffer by the down projection, reduction + broadcast kernel), match one
+GPU within tolerance on every rank's block and on the broadcast full output;
+token shards are bit-identical to the single-GPU forward of the same tokens."""
 from __future__ import annotations
 
 import os
@@ -53,8 +55,16 @@ def _worker(rank, world, port, queue):
         tok = ops.mlp_forward(x[lo:hi].contiguous(), full[0].w_in, full[0].b_in, full[0].w_out, full[0].b_out, gate)
         whole = ops.mlp_forward(x, full[0].w_in, full[0].b_in, full[0].w_out, full[0].b_out, gate)
         same = bool(torch.equal(tok, whole[lo:hi]))
+        # the fused d_ff split: P2P scatter from the down projection, reduction + broadcast kernel
+        fused = sdist.FusedDffSplit(layers, t)
+        y_fused = fused.forward(x)
+        err_fused = omlp.max_rel_error(y_fused.float().cpu(), ref[lo:hi].float().cpu())
+        full_x = fused.x.clone()
+        y_again = fused.forward(x).clone()  # a second call reuses the buffers and gives the same result
+        same_again = bool(torch.equal(y_again, y_fused)) and bool(torch.equal(fused.x, full_x))
+        rows_ok = omlp.max_rel_error(full_x.float().cpu(), ref.float().cpu())  # every block reached every rank
         torch.cuda.synchronize(dev)
-        queue.put((rank, err, same, ops.device_status(rank)))
+        queue.put((rank, err, same, ops.device_status(rank), err_fused, same_again, rows_ok))
     finally:
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
@@ -73,7 +83,10 @@ def test_dff_split_over_nccl_and_token_shards():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, err, same, status in results:
+    for rank, err, same, status, err_fused, same_again, rows_ok in results:
         assert err <= 2e-2, (rank, err)  # fp16 partials summed by NCCL, then bias and residual rounding
         assert same
         assert status == 0
+        assert err_fused <= 2e-2, (rank, err_fused)  # fp16 partials summed in fp32
+        assert same_again
+        assert rows_ok <= 2e-2, (rank, rows_ok)
