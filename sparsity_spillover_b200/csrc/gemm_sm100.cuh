@@ -781,22 +781,29 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
             if (ball & 0x0000ffffu) nz_bits |= 1u << (2 * grp);
             if (ball & 0xffff0000u) nz_bits |= 1u << (2 * grp + 1);
           }
+          // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) in this warp's tile slab.
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
+                make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
           if (scatter) {
-            // The partial chunk goes straight to its token block's owner (peer memory over NVLink).
-            if (row_ok) {
-              const int owner = row / p.scatter_rows;
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.scatter_out[owner]) +
-                                                    static_cast<size_t>(row - owner * p.scatter_rows) * p.N + col0);
+            // The partial chunk goes to its token block's owner (peer memory over
+            // NVLink), read back from the slab so that one store instruction writes
+            // eight whole 64-byte row segments: lane l moves 16 bytes of row l / 4.
+            __syncwarp();
+            const int owner = row0 / p.scatter_rows;  // token blocks hold whole tiles
+            uint16_t* dst_base = static_cast<uint16_t*>(p.scatter_out[owner]) +
+                                 static_cast<size_t>(row0 - owner * p.scatter_rows) * p.N + col0;
+            const int piece = lane & 3;
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
-                dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+            for (int i = 0; i < 4; ++i) {
+              const int r = 8 * i + (lane >> 2);
+              if (row0 + r < p.M) {
+                const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + ((piece ^ ((r >> 1) & 3)) << 4));
+                *reinterpret_cast<uint4*>(dst_base + static_cast<size_t>(r) * p.N + piece * 8) = v;
+              }
             }
-          } else {
-            // Stage the 32x32 chunk (64-byte rows, 64-byte swizzle) in this warp's tile slab.
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              *reinterpret_cast<uint4*>(buf + lane * 64 + ((c ^ sw) << 4)) =
-                  make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+            __syncwarp();  // the slot is rewritten by the next chunk
           }
         }
         if (scatter) return;  // nothing staged for a TMA store
