@@ -64,6 +64,7 @@ extern "C" {
 #define SPMLP_EALIGN -3   /* pointer not 16-byte aligned                              */
 #define SPMLP_EDEVICE -4  /* current device is not an sm_100 GPU                      */
 #define SPMLP_EDRIVER -5  /* tensor-map encoding unavailable or failed                */
+#define SPMLP_EFORMAT -6  /* serialized mask malformed, truncated or checksum mismatch */
 
 /* Tile bitmap geometry.  Bit (g % 32) of word [r * words + g / 32] is set iff
  * the 16-token x 64-feature tile (rows 16r.., features 64g..) of h holds a
@@ -71,6 +72,26 @@ extern "C" {
  * ceil(T/16) * words uint32 words. */
 int spmlp_tile_bits_words(int F);
 int64_t spmlp_tile_bits_size(int64_t T, int F);
+
+/* Persisted tile bitmaps (host memory, no GPU needed).  No counterpart in the
+ * reference, which recomputes its masks on every forward; this is the format
+ * for keeping a bitmap across calls or processes (e.g. a cached prefill).  The
+ * byte string is self-describing: a 64-byte header ("SPMB", version 1,
+ * encoding, 16x64 tile geometry, T, F, words per row group, CRC-32 of the
+ * payload, payload bytes, live tiles) and the payload.
+ *   SPMLP_MASK_RAW:      the bitmap words as above.
+ *   SPMLP_MASK_ROW_RUNS: runs of identical 16-row groups (u32 run count, then
+ *                        per run a u32 length and the group's words); lossless.
+ *                        Element-random masks (all groups alike) become one run,
+ *                        token-blocked masks shrink by their block height.
+ * encode returns the bytes written; decode rebuilds the exact words and rejects
+ * malformed or corrupted input with SPMLP_EFORMAT. */
+#define SPMLP_MASK_RAW 0
+#define SPMLP_MASK_ROW_RUNS 1
+int64_t spmlp_mask_encoded_size(const uint32_t* tile_bits, int64_t T, int F, int encoding);
+int64_t spmlp_mask_encode(const uint32_t* tile_bits, int64_t T, int F, int encoding, void* out, int64_t capacity);
+int spmlp_mask_decode_header(const void* data, int64_t n, int64_t* T, int* F, int* encoding);
+int spmlp_mask_decode(const void* data, int64_t n, uint32_t* tile_bits, int64_t capacity_words);
 
 /* Tile bitmap of an existing h [T,F] (same bit semantics as spmlp_up_gate's;
  * for callers whose h does not come from spmlp_up_gate).  Overwrites every

@@ -22,6 +22,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_tile_bits_words": (I32, [I32]),
     "spmlp_down_tile_tokens": (I32, [I32]),
     "spmlp_tile_bits_size": (I64, [I64, I32]),
+    "spmlp_mask_encoded_size": (I64, [VP, I64, I32, I32]),
+    "spmlp_mask_encode": (I64, [VP, I64, I32, I32, VP, I64]),
+    "spmlp_mask_decode_header": (I32, [VP, I64, _c.POINTER(I64), _c.POINTER(I32), _c.POINTER(I32)]),
+    "spmlp_mask_decode": (I32, [VP, I64, VP, I64]),
     "spmlp_tile_bits_from_h": (I32, [VP, VP, I64, I32, I32, VP]),
     "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
     "spmlp_down_sparse": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
@@ -43,6 +47,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 F16, BF16 = 0, 1
 GATE_IDENTITY, GATE_GELU, GATE_ONE_SIDED, GATE_SYMMETRIC, GATE_RELU, GATE_GELU_MASKED, GATE_CORNER = range(7)
 DOWN_DENSE, DOWN_SKIP, DOWN_SKIP_FINE = 0, 1, 2
+MASK_RAW, MASK_ROW_RUNS = 0, 1
 HEAD_GATE_NONE, HEAD_GATE_K, HEAD_GATE_N = 0, 1, 2
 
 _lib: ctypes.CDLL | None = None
@@ -85,6 +90,15 @@ def call(name: str, *args) -> None:
     rc = getattr(lib, name)(*args)
     if rc != 0:
         raise SpmlpError(name, rc, lib.spmlp_last_error().decode(errors="replace"))
+
+
+def call_size(name: str, *args) -> int:
+    """Call an entry point that returns a byte count; raise SpmlpError when it is negative."""
+    lib = load()
+    n = getattr(lib, name)(*args)
+    if n < 0:
+        raise SpmlpError(name, n, lib.spmlp_last_error().decode(errors="replace"))
+    return n
 
 
 def exported_symbols() -> list[str]:

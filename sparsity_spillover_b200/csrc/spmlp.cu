@@ -15,6 +15,7 @@
 #include "head_prepare.cuh"
 #include "bitmap.cuh"
 #include "collective.cuh"
+#include "mask_format.cuh"
 #include "spmlp.h"
 
 namespace spmlp {
@@ -657,6 +658,114 @@ int spmlp_tile_bits_words(int F) {
 int64_t spmlp_tile_bits_size(int64_t T, int F) {
   if (T <= 0 || F <= 0) return 0;
   return ((T + kBitsRows - 1) / kBitsRows) * static_cast<int64_t>(spmlp_tile_bits_words(F));
+}
+
+static int check_mask_geometry(int64_t T, int F, int encoding) {
+  if (T < 1 || T >= (int64_t(1) << 40)) return fail(SPMLP_ESHAPE, "T=%lld must be in [1, 2^40)", (long long)T);
+  if (F < kBitsCols || F % kBitsCols || F / kBitsCols > 65536)
+    return fail(SPMLP_ESHAPE, "F=%d must be a positive multiple of 64 with at most 65536 tiles", F);
+  if (encoding != SPMLP_MASK_RAW && encoding != SPMLP_MASK_ROW_RUNS)
+    return fail(SPMLP_EINVAL, "unknown mask encoding %d", encoding);
+  return 0;
+}
+
+int64_t spmlp_mask_encoded_size(const uint32_t* tile_bits, int64_t T, int F, int encoding) {
+  int rc;
+  if (!tile_bits) return fail(SPMLP_EINVAL, "tile_bits must be non-null");
+  if ((rc = check_mask_geometry(T, F, encoding))) return rc;
+  return mask::kHeaderBytes + mask::payload_bytes(tile_bits, T, spmlp_tile_bits_words(F), encoding);
+}
+
+int64_t spmlp_mask_encode(const uint32_t* tile_bits, int64_t T, int F, int encoding, void* out, int64_t capacity) {
+  const int64_t size = spmlp_mask_encoded_size(tile_bits, T, F, encoding);
+  if (size < 0) return size;
+  if (!out) return fail(SPMLP_EINVAL, "out must be non-null");
+  if (capacity < size) return fail(SPMLP_ESHAPE, "out holds %lld bytes, %lld needed", (long long)capacity, (long long)size);
+  const int words = spmlp_tile_bits_words(F);
+  uint8_t* o = static_cast<uint8_t*>(out);
+  uint8_t* payload = o + mask::kHeaderBytes;
+  mask::write_payload(tile_bits, T, words, encoding, payload);
+  const int64_t pbytes = size - mask::kHeaderBytes;
+  std::memset(o, 0, mask::kHeaderBytes);
+  mask::put<uint32_t>(o + 0, mask::kMagic);
+  mask::put<uint16_t>(o + 4, mask::kVersion);
+  mask::put<uint16_t>(o + 6, static_cast<uint16_t>(encoding));
+  mask::put<uint16_t>(o + 8, static_cast<uint16_t>(kBitsRows));
+  mask::put<uint16_t>(o + 10, static_cast<uint16_t>(kBitsCols));
+  mask::put<uint32_t>(o + 12, static_cast<uint32_t>(F));
+  mask::put<uint64_t>(o + 16, static_cast<uint64_t>(T));
+  mask::put<uint32_t>(o + 24, static_cast<uint32_t>(words));
+  mask::put<uint32_t>(o + 28, mask::crc32(payload, static_cast<size_t>(pbytes)));
+  mask::put<uint64_t>(o + 32, static_cast<uint64_t>(pbytes));
+  mask::put<uint64_t>(o + 40, static_cast<uint64_t>(mask::popcount_all(tile_bits, mask::groups_of(T) * words)));
+  return size;
+}
+
+int spmlp_mask_decode_header(const void* data, int64_t n, int64_t* T, int* F, int* encoding) {
+  if (!data) return fail(SPMLP_EINVAL, "data must be non-null");
+  const uint8_t* b = static_cast<const uint8_t*>(data);
+  if (n < mask::kHeaderBytes || mask::get<uint32_t>(b) != mask::kMagic)
+    return fail(SPMLP_EFORMAT, "not a serialized tile bitmap (bad magic or short header)");
+  if (mask::get<uint16_t>(b + 4) != mask::kVersion)
+    return fail(SPMLP_EFORMAT, "unsupported mask format version %u", unsigned(mask::get<uint16_t>(b + 4)));
+  if (mask::get<uint16_t>(b + 8) != kBitsRows || mask::get<uint16_t>(b + 10) != kBitsCols)
+    return fail(SPMLP_EFORMAT, "mask tiles are %ux%u, this library uses %dx%d", unsigned(mask::get<uint16_t>(b + 8)),
+                unsigned(mask::get<uint16_t>(b + 10)), kBitsRows, kBitsCols);
+  const int enc = mask::get<uint16_t>(b + 6);
+  const int64_t t = static_cast<int64_t>(mask::get<uint64_t>(b + 16));
+  const uint32_t f = mask::get<uint32_t>(b + 12);
+  if (f > 0x7fffffffu || check_mask_geometry(t, static_cast<int>(f), enc))
+    return fail(SPMLP_EFORMAT, "mask header holds an invalid shape or encoding");
+  if (static_cast<int>(mask::get<uint32_t>(b + 24)) != spmlp_tile_bits_words(static_cast<int>(f)))
+    return fail(SPMLP_EFORMAT, "mask header word count does not match F");
+  const uint64_t pbytes = mask::get<uint64_t>(b + 32);
+  if (pbytes > static_cast<uint64_t>(n - mask::kHeaderBytes)) return fail(SPMLP_EFORMAT, "mask payload is truncated");
+  if (T) *T = t;
+  if (F) *F = static_cast<int>(f);
+  if (encoding) *encoding = enc;
+  return 0;
+}
+
+int spmlp_mask_decode(const void* data, int64_t n, uint32_t* tile_bits, int64_t capacity_words) {
+  int64_t T = 0;
+  int F = 0, enc = 0;
+  int rc = spmlp_mask_decode_header(data, n, &T, &F, &enc);
+  if (rc) return rc;
+  if (!tile_bits) return fail(SPMLP_EINVAL, "tile_bits must be non-null");
+  const uint8_t* b = static_cast<const uint8_t*>(data);
+  const uint8_t* payload = b + mask::kHeaderBytes;
+  const int64_t pbytes = static_cast<int64_t>(mask::get<uint64_t>(b + 32));
+  if (mask::crc32(payload, static_cast<size_t>(pbytes)) != mask::get<uint32_t>(b + 28))
+    return fail(SPMLP_EFORMAT, "mask payload checksum mismatch");
+  const int words = spmlp_tile_bits_words(F);
+  const int64_t groups = mask::groups_of(T);
+  if (capacity_words < groups * words)
+    return fail(SPMLP_ESHAPE, "tile_bits holds %lld words, %lld needed", (long long)capacity_words,
+                (long long)(groups * words));
+  if (enc == SPMLP_MASK_RAW) {
+    if (pbytes != groups * words * 4) return fail(SPMLP_EFORMAT, "raw mask payload has the wrong size");
+    std::memcpy(tile_bits, payload, static_cast<size_t>(pbytes));
+  } else {
+    if (pbytes < 4) return fail(SPMLP_EFORMAT, "row-run mask payload is truncated");
+    const int64_t runs = mask::get<uint32_t>(payload);
+    if (4 + runs * (1 + words) * 4 != pbytes) return fail(SPMLP_EFORMAT, "row-run mask payload has the wrong size");
+    const uint8_t* o = payload + 4;
+    int64_t r = 0;
+    for (int64_t i = 0; i < runs; ++i, o += (1 + words) * 4) {
+      const int64_t len = mask::get<uint32_t>(o);
+      if (len < 1 || len > groups - r) return fail(SPMLP_EFORMAT, "row runs do not cover the token groups");
+      for (int64_t k = 0; k < len; ++k, ++r) std::memcpy(tile_bits + r * words, o + 4, static_cast<size_t>(words) * 4);
+    }
+    if (r != groups) return fail(SPMLP_EFORMAT, "row runs do not cover the token groups");
+  }
+  // Bits past the last 64-feature tile of a group must be clear.
+  const int tiles = F / kBitsCols;
+  if (tiles % 32) {
+    const uint32_t spare = ~((1u << (tiles % 32)) - 1u);
+    for (int64_t r = 0; r < groups; ++r)
+      if (tile_bits[r * words + words - 1] & spare) return fail(SPMLP_EFORMAT, "mask sets bits past the last tile");
+  }
+  return 0;
 }
 
 int spmlp_tile_bits_from_h(const void* h, uint32_t* tile_bits, int64_t T, int F, int dtype, void* stream) {

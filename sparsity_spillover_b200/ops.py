@@ -84,6 +84,50 @@ def tile_bits_from_h(h: torch.Tensor, bits: torch.Tensor | None = None) -> torch
     return bits
 
 
+_MASK_ENCODINGS = {"raw": _lib.MASK_RAW, "runs": _lib.MASK_ROW_RUNS}
+
+
+def encode_mask(bits: torch.Tensor, tokens: int, features: int, encoding: str = "raw") -> bytes:
+    """Serialise a 16x64 tile bitmap (device or host int32[tile_bits_size(T, F)]) into the
+    self-describing byte format of include/spmlp.h: "raw" words or lossless "runs" of
+    identical 16-row groups."""
+    if encoding not in _MASK_ENCODINGS:
+        raise ValueError(f"encoding must be one of {sorted(_MASK_ENCODINGS)}")
+    host = bits.detach().to("cpu", torch.int32).contiguous()
+    if host.numel() != tile_bits_size(tokens, features):
+        raise ValueError("bits does not match tile_bits_size(tokens, features)")
+    code = _MASK_ENCODINGS[encoding]
+    size = _lib.call_size("spmlp_mask_encoded_size", host.data_ptr(), tokens, features, code)
+    out = (ctypes.c_uint8 * size)()
+    _lib.call_size("spmlp_mask_encode", host.data_ptr(), tokens, features, code, ctypes.addressof(out), size)
+    return bytes(out)
+
+
+def decode_mask(data: bytes, device: torch.device | str | None = None) -> tuple[torch.Tensor, int, int]:
+    """(bits, T, F) from a serialised bitmap; bits on ``device`` (host when None)."""
+    buf = ctypes.create_string_buffer(bytes(data), len(data))
+    t, f, enc = ctypes.c_int64(0), ctypes.c_int(0), ctypes.c_int(0)
+    _lib.call("spmlp_mask_decode_header", ctypes.addressof(buf), len(data), ctypes.byref(t), ctypes.byref(f),
+              ctypes.byref(enc))
+    bits = torch.empty(tile_bits_size(t.value, f.value), dtype=torch.int32)
+    _lib.call("spmlp_mask_decode", ctypes.addressof(buf), len(data), bits.data_ptr(), bits.numel())
+    return (bits if device is None else bits.to(device)), t.value, f.value
+
+
+def save_mask(path, bits: torch.Tensor, tokens: int, features: int, encoding: str = "raw") -> int:
+    """Write a tile bitmap to ``path``; returns the bytes written."""
+    data = encode_mask(bits, tokens, features, encoding)
+    with open(path, "wb") as fh:
+        fh.write(data)
+    return len(data)
+
+
+def load_mask(path, device: torch.device | str | None = None) -> tuple[torch.Tensor, int, int]:
+    """(bits, T, F) read from a file written by ``save_mask``."""
+    with open(path, "rb") as fh:
+        return decode_mask(fh.read(), device)
+
+
 def up_gate(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, gate=None, *,
             h: torch.Tensor | None = None, bits: torch.Tensor | None = None, z_out: torch.Tensor | None = None,
             seq_len: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:

@@ -316,3 +316,22 @@ def test_streamed_host_batches_match_device_forward():
         torch.cuda.synchronize()
         for y, e in zip(y_hosts, expect):
             assert torch.equal(y, e)
+
+
+@pytest.mark.parametrize("encoding", ["raw", "runs"])
+def test_persisted_bitmap_drives_the_down_projection_identically(tmp_path, encoding):
+    """A bitmap saved to disk and loaded back skips exactly the same K-tiles."""
+    from sparsity_spillover_b200 import ops, workloads
+
+    t, f, d = 8192, 2048, 512
+    h, _ = workloads.tile_structured_h(t, f, 0.2, seed=31, device="cuda")
+    w = (torch.randn(d, f, device="cuda") * 0.02).to(h.dtype)
+    bits = ops.tile_bits_from_h(h)
+    ops.save_mask(tmp_path / "mask.spmb", bits, t, f, encoding)
+    loaded, t2, f2 = ops.load_mask(tmp_path / "mask.spmb", device="cuda")
+    assert (t2, f2) == (t, f) and torch.equal(loaded, bits)
+    st_a = torch.zeros(2, dtype=torch.int64, device="cuda")
+    st_b = torch.zeros(2, dtype=torch.int64, device="cuda")
+    y_a = ops.down_sparse(h, bits, w, None, stats=st_a)
+    y_b = ops.down_sparse(h, loaded, w, None, stats=st_b)
+    assert torch.equal(y_a, y_b) and torch.equal(st_a, st_b) and int(st_a[1]) > 0
