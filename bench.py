@@ -429,6 +429,14 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
     return out
 
 
+def _extra(fn, *args):
+    """A secondary measurement: its failure is recorded in the JSON line, never fatal to it."""
+    try:
+        return fn(*args)
+    except Exception as exc:  # noqa: BLE001 - reported, not hidden
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+
 def time_device(fn, steps: int, device) -> float:
     import torch
 
@@ -625,16 +633,16 @@ def run_ours(args):
         "device_status": status,
     }
     if world > 1 and not args.no_extras:
-        line["dff_split_cfg3"] = dff_split_measure(device, world, rank)
+        line["dff_split_cfg3"] = _extra(dff_split_measure, device, world, rank)
     if world == 1 and not args.no_extras:
         import torch
 
         with torch.inference_mode():
-            line["density_sweep"] = density_sweep(device)
-            line["tile_structured_cfg2"] = tile_structured(device)
-            line["pythia410m_cfg3"] = cfg3_410m(device)
-            line["vocab_head_cfg4"] = head_bench(device)
-            line["joint_cfg1"] = joint_cfg1(device)
+            line["density_sweep"] = _extra(density_sweep, device)
+            line["tile_structured_cfg2"] = _extra(tile_structured, device)
+            line["pythia410m_cfg3"] = _extra(cfg3_410m, device)
+            line["vocab_head_cfg4"] = _extra(head_bench, device)
+            line["joint_cfg1"] = _extra(joint_cfg1, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
     if world > 1:
