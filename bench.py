@@ -331,6 +331,43 @@ def head_bench(device, steps=5) -> list[dict]:
     return rows
 
 
+def layernorm_fold_cfg1(device, steps: int = 10) -> dict:
+    """post_attention_layernorm + up projection + gate on a cfg1 layer (T=32768, d=512,
+    F=2048, fp16): torch's LayerNorm followed by up_gate, against the LayerNorm folded
+    into the up projection (row statistics + up_gate_ln; the normalized activation is
+    never written); each captured as a CUDA graph."""
+    import torch
+
+    from sparsity_spillover_b200 import ops, workloads
+
+    cfg = workloads.CONFIGS["cfg1"]
+    layer = workloads.make_weights(cfg, device)[0]
+    x = workloads.make_input(cfg, device) + 2.0
+    ln = torch.nn.LayerNorm(cfg.d, eps=1e-5).to(device=device, dtype=cfg.dtype)
+    with torch.no_grad():
+        ln.weight.normal_(1.0, 0.1)
+        ln.bias.normal_(0.0, 0.1)
+    gate = {"operator": "one_sided_threshold", "kappa": 0.05}
+    fold = ops.FoldedLayerNorm(ln.weight, ln.bias, ln.eps, layer.w_in, layer.b_in)
+    t, f = x.shape[0], cfg.F
+    h = torch.empty(t, f, dtype=cfg.dtype, device=device)
+    bits = torch.empty(ops.tile_bits_size(t, f), dtype=torch.int32, device=device)
+    stats = (torch.empty(t, device=device), torch.empty(t, device=device))
+
+    def unfused():
+        ops.up_gate(ln(x), layer.w_in, layer.b_in, gate, h=h, bits=bits)
+
+    def fused():
+        ops.row_stats(x, ln.eps, *stats)
+        ops.up_gate_ln(x, fold, gate, h=h, bits=bits, stats=stats)
+
+    t_un = time_device(graph_of(unfused, device).replay, steps, device)
+    t_fu = time_device(graph_of(fused, device).replay, steps, device)
+    t_st = time_device(lambda: ops.row_stats(x, ln.eps, *stats), steps, device)
+    return {"tokens": t, "d": cfg.d, "F": f, "layernorm_then_up_gate_us": t_un * 1e6, "folded_us": t_fu * 1e6,
+            "row_stats_us": t_st * 1e6, "speedup": t_un / t_fu}
+
+
 def joint_cfg1(device, steps: int = 10) -> dict:
     """The joint consumer on the cfg1 layer shape (T=32768, d=512, F=2048, fp16; h from
     up_gate at 10 % element density, attention context z ~ N(0,1), residual x):
@@ -643,6 +680,7 @@ def run_ours(args):
             line["pythia410m_cfg3"] = _extra(cfg3_410m, device)
             line["vocab_head_cfg4"] = _extra(head_bench, device)
             line["joint_cfg1"] = _extra(joint_cfg1, device)
+            line["layernorm_fold_cfg1"] = _extra(layernorm_fold_cfg1, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
     if world > 1:

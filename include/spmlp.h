@@ -113,6 +113,24 @@ int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, ui
                   void* z_out, int64_t T, int d, int F, int dtype, int gate_op, float kappa,
                   int64_t seq_len, void* stream);
 
+/* Up projection with the MLP's LayerNorm folded in, so that the normalized
+ * activation m = post_attention_layernorm(x) is never materialised.  Replaces
+ * the reference's paired LayerNorm (runs/035-2026-09-18-pythia70m-k050-port/kernel/norm/norm.cu:23-60,
+ * its MLP output m) followed by dense_h_to_4h + gate.
+ *   spmlp_row_stats: per token of x [T,d], mean and rstd = 1/sqrt(var + eps)
+ *   (fp32, biased variance as torch.nn.LayerNorm).
+ *   spmlp_up_gate_ln: as spmlp_up_gate on the raw x with w_fold = W_in diag(gamma)
+ *   [F,d] in the activation dtype, ln_s[f] = sum_k w_fold[f,k] and
+ *   ln_c = b_in + W_in beta (fp32 [F]):
+ *     z = round(rstd * (x w_fold^T - mean * ln_s) + ln_c), then the gate, bitmap
+ *     and optional z export as spmlp_up_gate.
+ *   z differs from the unfused round(round(LN(x)) W_in^T + b_in) by the rounding
+ *   of m that the fold skips. */
+int spmlp_row_stats(const void* x, float* mean, float* rstd, int64_t T, int d, int dtype, float eps, void* stream);
+int spmlp_up_gate_ln(const void* x, const void* w_fold, const float* ln_s, const float* ln_c, const float* row_mean,
+                     const float* row_rstd, void* h, uint32_t* tile_bits, void* z_out, int64_t T, int d, int F,
+                     int dtype, int gate_op, float kappa, int64_t seq_len, void* stream);
+
 /* Sparse down-projection.  Replaces GPTNeoXMLP.dense_4h_to_h and the h branch
  * of the reference's joint consumer (runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:138-157,
  * adapter call runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/candidate.py:26-33).

@@ -74,6 +74,16 @@ def joint(h, z, w2, b2, wo, bo, residual, th: float, tz: float, gh: bool, gz: bo
     return (s.float() + residual.float()).to(dtype)
 
 
+def layer_norm_linear(x, gamma, beta, eps: float, w, b):
+    """fp32 dense_h_to_4h(post_attention_layernorm(x)) of a GPT-NeoX layer
+    (transformers GPTNeoXLayer.forward; the reference's paired LayerNorm,
+    runs/035-2026-09-18-pythia70m-k050-port/kernel/norm/norm.cu:23-60, produces the
+    same m).  m is kept in fp32 here, as the folded kernel does not round it."""
+    m = torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), None if gamma is None else gamma.float(),
+                                       None if beta is None else beta.float(), eps)
+    return linear(m, w, b)
+
+
 def max_rel_error(actual: torch.Tensor, reference: torch.Tensor) -> float:
     """max|actual - reference| / max|reference| — the tolerance metric of the north star."""
     a, r = actual.double(), reference.double()

@@ -28,6 +28,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_mask_decode": (I32, [VP, I64, VP, I64]),
     "spmlp_tile_bits_from_h": (I32, [VP, VP, I64, I32, I32, VP]),
     "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
+    "spmlp_row_stats": (I32, [VP, VP, VP, I64, I32, I32, F32, VP]),
+    "spmlp_up_gate_ln": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
     "spmlp_down_sparse": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_down_scatter": (I32, [VP, VP, VP, _c.POINTER(VP), I32, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_reduce_broadcast": (I32, [VP, I32, I64, I32, VP, VP, _c.POINTER(VP), I32, I32, VP]),

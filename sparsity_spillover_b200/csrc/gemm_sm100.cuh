@@ -63,6 +63,13 @@ struct GemmParams {
   const void* residual;   // KIND_DOWN / KIND_JOINT: optional [M, N]
   int K2;                 // KIND_JOINT: reduction length of the second product (z Wo^T)
   const void* bias2;      // KIND_JOINT: [N] bias of the second product, nullable
+  // KIND_UP with a LayerNorm folded into the weight (B = W diag(gamma)): z =
+  // round(rstd[m] * (acc - mean[m] * ln_s[n]) + ln_c[n]) instead of round(acc + b),
+  // with ln_s = sum_k B[n, k] and ln_c = b + W beta (fp32).  Null: no LayerNorm.
+  const float* ln_mean;   // [M]
+  const float* ln_rstd;   // [M]
+  const float* ln_s;      // [N]
+  const float* ln_c;      // [N]
   uint32_t* bits_out;     // KIND_UP: 16x64 tile bitmap, zeroed by the host
   const uint32_t* bits_in;  // KIND_DOWN / KIND_JOINT: 16x64 bitmap of A; KIND_HEAD: 16x16 support bits
   int bits_words;         // words per 16-row group in bits_out / bits_in
@@ -180,7 +187,10 @@ struct GemmTraits {
   static constexpr int kFlush = kWarpChunks < 4 ? kWarpChunks : 4;  // chunks per fence + store batch (RING = 0)
   static constexpr int kSlabChunks = RING > 0 ? RING : kWarpChunks;  // staged chunks per epilogue warp
   static constexpr uint32_t kEpiBytes = EPI * kSlabChunks * kStageOutBytes;
-  static constexpr uint32_t kBiasBytes = kAccs * EPI * kWarpChunks * 32 * 4;  // each warp's own columns, fp32
+  // Per-column fp32 vectors staged per warp: the bias (two for the joint; the
+  // up projection's folded LayerNorm uses two: ln_s and ln_c).
+  static constexpr int kColVecs = (KIND == KIND_JOINT || KIND == KIND_UP) ? 2 : 1;
+  static constexpr uint32_t kBiasBytes = kColVecs * EPI * kWarpChunks * 32 * 4;  // each warp's own columns
   static constexpr uint32_t kBarrierBytes = 256;
   static_assert((2 * STAGES + 5 + EPI) * 8 + 4 <= kBarrierBytes, "barrier region too small");
   static constexpr uint32_t kSmemBytes =
@@ -270,13 +280,25 @@ struct UpEpilogue {
   // z = round(acc + b) two values per word; h = gate(z) computed on packed
   // words: a comparison mask clears rejected halves (NaN compares false, so
   // masked_fill(z < kappa, 0) keeps it, as torch does).
+  // With a folded LayerNorm (ln_c non-null) `bias` holds ln_s and the row's mean
+  // and rstd are given.
   __device__ __forceinline__ static bool apply(const GemmParams& p, int row, int col0, int lane, bool row_ok,
                                                const uint32_t (&acc)[32], const float* bias, uint32_t k2,
-                                               uint32_t (&out)[16]) {
+                                               uint32_t (&out)[16], const float* ln_c = nullptr,
+                                               float mean = 0.f, float rstd = 0.f) {
     uint32_t z[16];
+    if (ln_c != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      z[j] = D::pack_rn(__uint_as_float(acc[2 * j]) + bias[2 * j], __uint_as_float(acc[2 * j + 1]) + bias[2 * j + 1]);
+      for (int j = 0; j < 16; ++j) {
+        const float a = fmaf(-mean, bias[2 * j], __uint_as_float(acc[2 * j]));
+        const float b = fmaf(-mean, bias[2 * j + 1], __uint_as_float(acc[2 * j + 1]));
+        z[j] = D::pack_rn(fmaf(rstd, a, ln_c[2 * j]), fmaf(rstd, b, ln_c[2 * j + 1]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        z[j] = D::pack_rn(__uint_as_float(acc[2 * j]) + bias[2 * j], __uint_as_float(acc[2 * j + 1]) + bias[2 * j + 1]);
+    }
     if constexpr (GATE == GATE_ONE_SIDED) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) out[j] = z[j] & ~D::lt_mask(z[j], k2);
@@ -610,7 +632,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     constexpr bool kRing = RING > 0;
     uint8_t* stage_out = s_out + ew * Tr::kSlabChunks * Tr::kStageOutBytes;
     float* bias_s = s_bias + ew * kMyChunks * 32;  // this warp's columns ch_begin*32 ..
-    float* bias2_s = bias_s + EPI * kMyChunks * 32;  // KIND_JOINT: the second product's bias
+    float* bias2_s = bias_s + EPI * kMyChunks * 32;  // KIND_JOINT: the second product's bias; KIND_UP: ln_c
+    const bool ln = KIND == KIND_UP && p.ln_c != nullptr;
     constexpr bool kHasRes = KIND == KIND_DOWN || KIND == KIND_JOINT;
     const bool with_res = kHasRes && p.residual != nullptr;
     const bool scatter = KIND == KIND_DOWN && p.scatter_rows > 0;
@@ -646,6 +669,26 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     };
     uint4 bias_next = load_bias(p.bias, unit);
     uint4 bias2_next = KIND == KIND_JOINT ? load_bias(p.bias2, unit) : make_uint4(0u, 0u, 0u, 0u);
+    // Folded LayerNorm: eight fp32 columns of ln_s and ln_c per lane, one tile ahead.
+    float4 lns_next[2], lnc_next[2];
+    auto load_ln = [&](int t) {
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      lns_next[0] = lns_next[1] = lnc_next[0] = lnc_next[1] = z;
+      if (ln && bias_lane && t < total_tiles) {
+        int mb, nc;
+        tile_coords<KIND, BN>(p, t, mb, nc);
+        const int col = nc + ch_begin * 32 + lane * 8;
+        if (col < p.N) {
+          const float4* sp = reinterpret_cast<const float4*>(p.ln_s + col);
+          const float4* cp = reinterpret_cast<const float4*>(p.ln_c + col);
+          lns_next[0] = __ldg(sp);
+          lns_next[1] = __ldg(sp + 1);
+          lnc_next[0] = __ldg(cp);
+          lnc_next[1] = __ldg(cp + 1);
+        }
+      }
+    };
+    if constexpr (KIND == KIND_UP) load_ln(unit);
 
     for (int t = unit; t < total_tiles; t += units) {
       int m_blk, n_col0;
@@ -656,6 +699,9 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const bool has_acc = KIND == KIND_JOINT || live_blocks > 0;  // the joint's z branch is never empty
+      // Folded LayerNorm: this thread's row statistics.
+      const float row_mean = (ln && row_ok) ? __ldg(p.ln_mean + row) : 0.f;
+      const float row_rstd = (ln && row_ok) ? __ldg(p.ln_rstd + row) : 0.f;
       const bool has_h = live_blocks > 0;                             // KIND_JOINT: the h accumulator was written
       const int ch_end = ch_begin + kMyChunks;
       // RING > 0: the residual of chunk ch (this thread's row, 32 values) into registers.
@@ -699,12 +745,20 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       if constexpr (KIND != KIND_HEAD) {
         __syncwarp();  // every lane is done with the previous tile's bias
         if (lane * 8 < kMyChunks * 32) {
-          store_bias(bias_next, bias_s + lane * 8);
+          if (ln) {
+            reinterpret_cast<float4*>(bias_s + lane * 8)[0] = lns_next[0];
+            reinterpret_cast<float4*>(bias_s + lane * 8)[1] = lns_next[1];
+            reinterpret_cast<float4*>(bias2_s + lane * 8)[0] = lnc_next[0];
+            reinterpret_cast<float4*>(bias2_s + lane * 8)[1] = lnc_next[1];
+          } else {
+            store_bias(bias_next, bias_s + lane * 8);
+          }
           if constexpr (KIND == KIND_JOINT) store_bias(bias2_next, bias2_s + lane * 8);
         }
         __syncwarp();
         bias_next = load_bias(p.bias, t + units);
         if constexpr (KIND == KIND_JOINT) bias2_next = load_bias(p.bias2, t + units);
+        if constexpr (KIND == KIND_UP) load_ln(t + units);
       }
 
       if (has_acc) {
@@ -753,7 +807,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           uint32_t packed[16];
           bool nz = false;
           if constexpr (KIND == KIND_UP) {
-            nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + slot * 32, k2, packed);
+            nz = UpEpilogue<BF16, GATE>::apply(p, row, col0, lane, row_ok, v, bias_s + slot * 32, k2, packed,
+                                               ln ? bias2_s + slot * 32 : nullptr, row_mean, row_rstd);
           } else if constexpr (KIND == KIND_DOWN) {
             uint4 r[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
                           make_uint4(0u, 0u, 0u, 0u)};

@@ -15,6 +15,7 @@
 #include "head_prepare.cuh"
 #include "bitmap.cuh"
 #include "collective.cuh"
+#include "layernorm.cuh"
 #include "mask_format.cuh"
 #include "spmlp.h"
 
@@ -249,8 +250,11 @@ int check_mk(int64_t T, int K, int N, const char* kname, const char* nname) {
 
 }  // namespace
 
+// ln_s != nullptr: the folded-LayerNorm form (w_in = W diag(gamma), b_in unused; see GemmParams).
 int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uint32_t* bits, void* z_out, int64_t T,
-                 int d, int F, int dtype, int gate_op, float kappa, int64_t seq_len, cudaStream_t stream) {
+                 int d, int F, int dtype, int gate_op, float kappa, int64_t seq_len, cudaStream_t stream,
+                 const float* ln_s = nullptr, const float* ln_c = nullptr, const float* ln_mean = nullptr,
+                 const float* ln_rstd = nullptr) {
   int rc;
   if (!x || !w_in || !h || !bits) return fail(SPMLP_EINVAL, "x, w_in, h and tile_bits must be non-null");
   if ((rc = check_dtype(dtype))) return rc;
@@ -258,6 +262,13 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   if ((rc = check_gate(gate_op, kappa, T, seq_len))) return rc;
   if (!aligned16(x) || !aligned16(w_in) || !aligned16(h) || (b_in && !aligned16(b_in)) || (z_out && !aligned16(z_out)))
     return fail(SPMLP_EALIGN, "x, w_in, b_in, h and z_out must be 16-byte aligned");
+  const bool ln = ln_s != nullptr;
+  if (ln) {
+    if (!ln_c || !ln_mean || !ln_rstd) return fail(SPMLP_EINVAL, "ln_s, ln_c, row_mean and row_rstd must be non-null");
+    if (!aligned16(ln_s) || !aligned16(ln_c)) return fail(SPMLP_EALIGN, "ln_s and ln_c must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(ln_mean) % 4 || reinterpret_cast<uintptr_t>(ln_rstd) % 4)
+      return fail(SPMLP_EALIGN, "row_mean and row_rstd must be 4-byte aligned");
+  }
   DeviceInfo* dev = nullptr;
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
@@ -276,7 +287,11 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   p.N = F;
   p.K = d;
   p.n_tiles = (F + BN - 1) / BN;
-  p.bias = b_in;
+  p.bias = ln ? nullptr : b_in;
+  p.ln_s = ln_s;
+  p.ln_c = ln_c;
+  p.ln_mean = ln_mean;
+  p.ln_rstd = ln_rstd;
   p.out = h;
   p.z_out = z_out;
   p.bits_out = bits;
@@ -400,6 +415,28 @@ int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w
   constexpr int S = kJointStages, E = kJointEpiWarps;
   if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
   return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+}
+
+int row_stats_impl(const void* x, float* mean, float* rstd, int64_t T, int d, int dtype, float eps,
+                   cudaStream_t stream) {
+  int rc;
+  if (!x || !mean || !rstd) return fail(SPMLP_EINVAL, "x, mean and rstd must be non-null");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T must be in [1, 2^31)");
+  if (d < kBK || d % kBK) return fail(SPMLP_ESHAPE, "d=%d must be a positive multiple of 64", d);
+  if (!std::isfinite(eps) || eps <= 0.f) return fail(SPMLP_EINVAL, "eps must be a finite positive number");
+  if (!aligned16(x)) return fail(SPMLP_EALIGN, "x must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int blocks = static_cast<int>((T + 7) / 8);  // eight tokens (warps) per 256-thread block
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  if (dtype == SPMLP_BF16)
+    row_stats_kernel<true><<<blocks, 256, 0, stream>>>(xs, mean, rstd, static_cast<int>(T), d, eps);
+  else
+    row_stats_kernel<false><<<blocks, 256, 0, stream>>>(xs, mean, rstd, static_cast<int>(T), d, eps);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "row_stats_kernel launch");
+  return 0;
 }
 
 int reduce_broadcast_impl(const void* recv, int world, int64_t rows, int d, const void* b_out, const void* residual,
@@ -776,6 +813,18 @@ int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, ui
                   int64_t T, int d, int F, int dtype, int gate_op, float kappa, int64_t seq_len, void* stream) {
   return up_gate_impl(x, w_in, b_in, h, tile_bits, z_out, T, d, F, dtype, gate_op, kappa, seq_len,
                       static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_row_stats(const void* x, float* mean, float* rstd, int64_t T, int d, int dtype, float eps, void* stream) {
+  return row_stats_impl(x, mean, rstd, T, d, dtype, eps, static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_up_gate_ln(const void* x, const void* w_fold, const float* ln_s, const float* ln_c, const float* row_mean,
+                     const float* row_rstd, void* h, uint32_t* tile_bits, void* z_out, int64_t T, int d, int F,
+                     int dtype, int gate_op, float kappa, int64_t seq_len, void* stream) {
+  if (!ln_s) return fail(SPMLP_EINVAL, "ln_s must be non-null");
+  return up_gate_impl(x, w_fold, nullptr, h, tile_bits, z_out, T, d, F, dtype, gate_op, kappa, seq_len,
+                      static_cast<cudaStream_t>(stream), ln_s, ln_c, row_mean, row_rstd);
 }
 
 int spmlp_down_sparse(const void* h, const uint32_t* tile_bits, const void* w_out, const void* b_out,

@@ -184,9 +184,6 @@ class FusedDffSplit:
         self.tokens, self.rows = tokens, tokens // self.world
         self.skip = skip
         group = self.group or dist.group.WORLD
-        if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(
-                group.group_name):
-            symm_mem.enable_symm_mem_for_group(group.group_name)
         self.x = symm_mem.empty((tokens, self.d), dtype=self.dtype, device=self.device)
         self.recv = symm_mem.empty((self.world, self.rows, self.d), dtype=self.dtype, device=self.device)
         hx = symm_mem.rendezvous(self.x, group)

@@ -191,6 +191,10 @@ class JointConsumer:
         self.skip = skip
         self.stats: torch.Tensor | None = None
         self._buffers: dict[str, torch.Tensor] = {}
+        # Set by install_joint: the up projection run by the fused layer forward.
+        self.up: torch.nn.Linear | None = None
+        self.up_gate: GateSpec | None = None
+        self.folded: ops.FoldedLayerNorm | None = None
 
     def _buffer(self, name: str, shape: tuple[int, ...], like: torch.Tensor, dtype: torch.dtype | None = None):
         dtype = dtype or like.dtype
@@ -241,19 +245,29 @@ def _joint_layer_forward(self, hidden_states, attention_mask=None, position_ids=
     z, _ = self.attention(self.input_layernorm(hidden_states), attention_mask=attention_mask,
                           position_ids=position_ids, layer_past=None, use_cache=False,
                           position_embeddings=position_embeddings, **kwargs)
-    m = self.post_attention_layernorm(hidden_states)
     joint = self._spmlp_joint
-    shape = m.shape
-    x = m.reshape(-1, shape[-1]).contiguous()
-    t, f = x.shape[0], joint.up.out_features
-    h = joint._buffer("h_up", (t, f), x)
-    bits = joint._buffer("bits_up", (ops.tile_bits_size(t, f),), x, torch.int32)
-    seq_len = shape[-2] if len(shape) >= 2 else t
-    ops.up_gate(x, joint.up.weight, joint.up.bias, joint.up_gate, h=h, bits=bits, seq_len=seq_len)
+    shape = hidden_states.shape
+    seq_len = shape[-2] if len(shape) >= 2 else None
+    if joint.folded is not None:
+        # post_attention_layernorm folded into the up projection: read the residual stream itself.
+        x = hidden_states.reshape(-1, shape[-1]).contiguous()
+        t, f = x.shape[0], joint.up.out_features
+        h = joint._buffer("h_up", (t, f), x)
+        bits = joint._buffer("bits_up", (ops.tile_bits_size(t, f),), x, torch.int32)
+        stats = (joint._buffer("ln_mean", (t,), x, torch.float32), joint._buffer("ln_rstd", (t,), x, torch.float32))
+        ops.row_stats(x, joint.folded.eps, *stats)
+        ops.up_gate_ln(x, joint.folded, joint.up_gate, h=h, bits=bits, seq_len=seq_len, stats=stats)
+    else:
+        m = self.post_attention_layernorm(hidden_states)
+        x = m.reshape(-1, shape[-1]).contiguous()
+        t, f = x.shape[0], joint.up.out_features
+        h = joint._buffer("h_up", (t, f), x)
+        bits = joint._buffer("bits_up", (ops.tile_bits_size(t, f),), x, torch.int32)
+        ops.up_gate(x, joint.up.weight, joint.up.bias, joint.up_gate, h=h, bits=bits, seq_len=seq_len)
     return joint.forward_gated(h, bits, z, hidden_states)
 
 
-def install_joint(model: torch.nn.Module, *, skip: bool | str = True) -> dict[str, Any]:
+def install_joint(model: torch.nn.Module, *, skip: bool | str = True, fuse_layernorm: bool = False) -> dict[str, Any]:
     """Fuse every parallel-residual layer's output side into one joint kernel.
 
     Per layer, as the reference's Adapter.install (k018 candidate.py:69-75): the
@@ -262,6 +276,9 @@ def install_joint(model: torch.nn.Module, *, skip: bool | str = True) -> dict[st
     projection its h branch, and ``layer.forward`` calls up_gate then the joint.
     The gate of h stays ``layer.mlp.act`` (applied by up_gate); a one-sided
     ``attention.z_gate`` is applied to z by the joint and bypassed inside attention.
+    With ``fuse_layernorm`` the MLP's post_attention_layernorm is folded into the up
+    projection (``ops.FoldedLayerNorm``, prepared here once), so its output is never
+    materialised; z then skips the rounding of the normalized activation.
     """
     layers = getattr(getattr(model, "gpt_neox", None), "layers", None)
     if layers is None:
@@ -274,10 +291,13 @@ def install_joint(model: torch.nn.Module, *, skip: bool | str = True) -> dict[st
         joint = JointConsumer(layer, skip=skip)
         joint.up = mlp.dense_h_to_4h
         joint.up_gate = mlp.gate if isinstance(mlp, SparseGPTNeoXMLP) else resolve(getattr(mlp, "act", None))
+        joint.folded = (ops.FoldedLayerNorm.from_modules(layer.post_attention_layernorm, joint.up)
+                        if fuse_layernorm else None)
         layer._spmlp_joint = joint
         layer.attention.dense = torch.nn.Identity()
         if joint.gz:
             layer.attention.z_gate.forward = MethodType(lambda self, x: x, layer.attention.z_gate)
         layer.forward = MethodType(_joint_layer_forward, layer)
         gates.append({"h": joint.up_gate.metadata(), "z": joint.z_gate.metadata() if joint.gz else None})
-    return {"joint": "spmlp up_gate + joint (sm_100a tcgen05)", "skip": skip, "gates": gates}
+    return {"joint": "spmlp up_gate + joint (sm_100a tcgen05)", "skip": skip, "fuse_layernorm": fuse_layernorm,
+            "gates": gates}

@@ -160,6 +160,80 @@ def up_gate(x: torch.Tensor, w_in: torch.Tensor, b_in: torch.Tensor | None, gate
     return h, bits
 
 
+class FoldedLayerNorm:
+    """A LayerNorm folded into the linear layer it feeds (weight preparation, done once).
+
+    For z = LN(x) W^T + b with LN(x) = (x - mean) * rstd * gamma + beta:
+    z = rstd * (x (W diag(gamma))^T - mean * s) + c with s[f] = sum_k (W diag(gamma))[f, k]
+    and c = b + W beta.  ``w_fold`` is stored in the activation dtype; ``s`` is summed
+    from the stored (rounded) ``w_fold`` so the mean subtraction matches what the GEMM
+    accumulates; ``s`` and ``c`` stay fp32.
+    """
+
+    def __init__(self, ln_weight: torch.Tensor | None, ln_bias: torch.Tensor | None, eps: float,
+                 weight: torch.Tensor, bias: torch.Tensor | None, dtype: torch.dtype | None = None):
+        dtype = dtype or weight.dtype
+        w = weight.detach().float()
+        gamma = torch.ones(w.shape[1], device=w.device) if ln_weight is None else ln_weight.detach().float()
+        beta = torch.zeros(w.shape[1], device=w.device) if ln_bias is None else ln_bias.detach().float()
+        self.w_fold = (w * gamma[None, :]).to(dtype).contiguous()
+        self.s = self.w_fold.float().sum(dim=1).contiguous()
+        c = w @ beta
+        if bias is not None:
+            c = c + bias.detach().float()
+        self.c = c.contiguous()
+        self.eps = float(eps)
+
+    @classmethod
+    def from_modules(cls, layer_norm: torch.nn.LayerNorm, linear: torch.nn.Linear, dtype=None) -> "FoldedLayerNorm":
+        return cls(layer_norm.weight, layer_norm.bias, layer_norm.eps, linear.weight, linear.bias, dtype)
+
+
+def row_stats(x: torch.Tensor, eps: float, mean: torch.Tensor | None = None,
+              rstd: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token LayerNorm statistics of x [T, d]: fp32 mean and 1/sqrt(var + eps)."""
+    device, dtype, code = _device_dtype(x)
+    t, d = x.shape
+    _check("x", x, dtype, device)
+    if mean is None:
+        mean = torch.empty(t, device=device, dtype=torch.float32)
+    if rstd is None:
+        rstd = torch.empty(t, device=device, dtype=torch.float32)
+    _check("mean", mean, torch.float32, device, (t,))
+    _check("rstd", rstd, torch.float32, device, (t,))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_row_stats", _ptr(x), _ptr(mean), _ptr(rstd), t, d, code, ctypes.c_float(eps), _stream(device))
+    return mean, rstd
+
+
+def up_gate_ln(x: torch.Tensor, folded: FoldedLayerNorm, gate=None, *, h: torch.Tensor | None = None,
+               bits: torch.Tensor | None = None, z_out: torch.Tensor | None = None, seq_len: int | None = None,
+               stats: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """h = gate(LN(x) W_in^T + b_in) with the LayerNorm folded in: reads the raw x [T, d]."""
+    spec = resolve(gate)
+    device, dtype, code = _device_dtype(x)
+    t, d = x.shape
+    f = folded.w_fold.shape[0]
+    _check("x", x, dtype, device)
+    _check("w_fold", folded.w_fold, dtype, device, (f, d))
+    _check("ln_s", folded.s, torch.float32, device, (f,))
+    _check("ln_c", folded.c, torch.float32, device, (f,))
+    mean, rstd = stats if stats is not None else row_stats(x, folded.eps)
+    if h is None:
+        h = torch.empty((t, f), device=device, dtype=dtype)
+    if bits is None:
+        bits = torch.empty((tile_bits_size(t, f),), device=device, dtype=torch.int32)
+    _check("h", h, dtype, device, (t, f))
+    _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+    if z_out is not None:
+        _check("z_out", z_out, dtype, device, (t, f))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_up_gate_ln", _ptr(x), _ptr(folded.w_fold), _ptr(folded.s), _ptr(folded.c), _ptr(mean),
+                  _ptr(rstd), _ptr(h), _ptr(bits), _ptr(z_out), t, d, f, code, spec.op,
+                  ctypes.c_float(spec.kappa_for(dtype)), int(seq_len or t), _stream(device))
+    return h, bits
+
+
 def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor, b_out: torch.Tensor | None,
                 residual: torch.Tensor | None = None, *, skip: bool | str = True, y: torch.Tensor | None = None,
                 stats: torch.Tensor | None = None) -> torch.Tensor:

@@ -108,6 +108,23 @@ def test_joint_consumer_reads_the_reference_gates():
         j(torch.zeros(64, 512), torch.zeros(64, 128), torch.zeros(64, 128))  # CPU tensors: no fallback
 
 
+def test_folded_layernorm_algebra_on_cpu():
+    """rstd * (x (W diag(gamma))^T - mean * s) + c == LN(x) W^T + b (weight preparation only)."""
+    from sparsity_spillover_b200 import ops
+
+    g = torch.Generator().manual_seed(4)
+    t, d, f = 64, 128, 256
+    x = torch.randn(t, d, generator=g, dtype=torch.float64) + 3.0
+    gamma, beta = 1 + 0.1 * torch.randn(d, generator=g), 0.1 * torch.randn(d, generator=g)
+    w, b = 0.05 * torch.randn(f, d, generator=g), 0.05 * torch.randn(f, generator=g)
+    fold = ops.FoldedLayerNorm(gamma, beta, 1e-5, w, b, dtype=torch.float32)
+    mean = x.mean(1, keepdim=True)
+    rstd = 1.0 / torch.sqrt(x.var(1, unbiased=False, keepdim=True) + 1e-5)
+    z = rstd * (x @ fold.w_fold.double().T - mean * fold.s.double()[None, :]) + fold.c.double()[None, :]
+    ref = torch.nn.functional.layer_norm(x, (d,), gamma.double(), beta.double(), 1e-5) @ w.double().T + b.double()
+    assert torch.allclose(z, ref, rtol=1e-5, atol=1e-5)
+
+
 def test_ops_refuse_cpu_tensors():
     from sparsity_spillover_b200 import ops
 
