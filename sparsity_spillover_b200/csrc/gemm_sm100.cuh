@@ -57,6 +57,11 @@ constexpr int kMaxRanks = 8;   // ranks a scattering down projection can address
 struct GemmParams {
   int M, N, K;            // tokens, output columns, reduction length
   int m_tiles, n_tiles;   // n_tiles = entries of col_tiles for KIND_HEAD
+  // Work items: tiles [0, tail_from) as they are, then each remaining tile as two
+  // half-width (BN/2-column) items, so the last round of a persistent grid is not
+  // left half idle.  work_items = tail_from + 2 * (m_tiles * n_tiles - tail_from).
+  int tail_from, work_items;
+  int split_tail;         // host: 1 = may split the last round's tiles (set from the launch shape)
   const void* bias;       // [N] in the activation dtype, nullable
   void* out;              // [M, N] row-major output (h, y or logits)
   void* z_out;            // KIND_UP: optional pre-gate z [M, N]
@@ -258,6 +263,22 @@ __device__ __forceinline__ void count_live(const GemmParams& p, int m_blk, int l
 }
 
 template <int KIND, int BN>
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_blk, int& n_col0);
+
+// Work item t -> its tile's M-block and first column; true for a half-width item.
+template <int KIND, int BN>
+__device__ __forceinline__ bool work_coords(const GemmParams& p, int t, int& m_blk, int& n_col0) {
+  if (t < p.tail_from) {
+    tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+    return false;
+  }
+  const int u = t - p.tail_from;
+  tile_coords<KIND, BN>(p, p.tail_from + (u >> 1), m_blk, n_col0);
+  n_col0 += (u & 1) * (BN / 2);
+  return true;
+}
+
+template <int KIND, int BN>
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_blk, int& n_col0) {
   m_blk = t / p.n_tiles;
   const int n_sel = t - m_blk * p.n_tiles;
@@ -400,7 +421,9 @@ struct JointEpilogue {
 // leader's single thread issues tcgen05.mma.cta_group::2 (M = 256) over both
 // CTAs' shared memory, and each CTA's TMEM receives its 128-row half.  Stage
 // completion is counted on the leader's barriers; commits multicast to both.
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0>
+// LN (KIND_UP only): the epilogue applies a LayerNorm folded into the weight
+// (GemmParams::ln_*); a compile-time switch so the plain up projection carries none of it.
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false>
 __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_r,
@@ -424,7 +447,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total_tiles = p.m_tiles * p.n_tiles;
+  const int total_tiles = p.work_items;  // work items (tiles, the tail split in halves)
   const uint32_t rank = (CG == 1) ? 0u : cluster_ctarank();
   const bool leader = rank == 0;
   const int unit = (CG == 1) ? static_cast<int>(blockIdx.x) : static_cast<int>(cluster_id_x());
@@ -469,9 +492,12 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     bool ok = true;
     for (int t = unit; t < total_tiles && ok; t += units) {
       int m_blk, n_col0;
-      tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+      const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
       const int a_row = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM;
-      const int b_row = n_col0 + static_cast<int>(rank) * (BN / CG);
+      const int b_row = n_col0 + static_cast<int>(rank) * ((half ? BN / 2 : BN) / CG);
+      // A half-width item loads half of B through the second B map (a box of BN/2/CG rows).
+      const CUtensorMap* map_b = half ? &tm_b2 : &tm_b;
+      const uint32_t stage_bytes = half ? Tr::kABytes + Tr::kBBytes / 2 : Tr::kStageBytes;
       // Load K-block kb of (ma, mb) into the next ring stage (warp-collective).
       auto issue = [&](const CUtensorMap* ma, const CUtensorMap* mb, int kb) -> bool {
         bool good = true;
@@ -479,12 +505,12 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           good = mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutProducer);
           if (good) {
             if constexpr (CG == 1) {
-              mbar_arrive_expect_tx(&full[stage], Tr::kStageBytes);
+              mbar_arrive_expect_tx(&full[stage], stage_bytes);
               tma_load_2d(s_a + stage * Tr::kABytes, ma, &full[stage], kb * kBK, a_row, 0ull);
               tma_load_2d(s_b + stage * Tr::kBBytes, mb, &full[stage], kb * kBK, b_row, pol_b);
             } else {
               // Both CTAs' bytes land on the leader's barrier; only the leader arrives.
-              if (leader) mbar_arrive_expect_tx(&full[stage], CG * Tr::kStageBytes);
+              if (leader) mbar_arrive_expect_tx(&full[stage], CG * stage_bytes);
               const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
               tma_load_2d_pair(s_a + stage * Tr::kABytes, ma, bar, kb * kBK, a_row, 0ull);
               tma_load_2d_pair(s_b + stage * Tr::kBBytes, mb, bar, kb * kBK, b_row, pol_b);
@@ -507,7 +533,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         if (!ok) break;
       }
       ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane,
-                                               [&](int kb, uint32_t) { return issue(&tm_a, &tm_b, kb); });
+                                               [&](int kb, uint32_t) { return issue(&tm_a, map_b, kb); });
     }
     if (!ok && lane == 0) {
       // Error path: let the copies this warp started land before the CTA exits.
@@ -537,7 +563,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (leader CTA only)
-    constexpr uint32_t idesc = umma_idesc_f16(Tr::kTileM, BN, BF16);
+    constexpr uint32_t idesc_full = umma_idesc_f16(Tr::kTileM, BN, BF16);
+    constexpr uint32_t idesc_half = umma_idesc_f16(Tr::kTileM, BN / 2, BF16);
     if (leader) {
       int stage = 0;
       uint32_t phase = 0;
@@ -548,11 +575,15 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const int k_steps_total = p.K / 16;
       for (int t = unit; t < total_tiles && ok; t += units) {
         int m_blk, n_col0;
-        tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+        const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
+        const uint32_t idesc = half ? idesc_half : idesc_full;
         int live_blocks, live_steps;
         count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
-        skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
-        issued_steps += static_cast<unsigned long long>(live_steps);
+        // Counted per whole tile: a split tile's second half adds nothing.
+        if (!half || ((t - p.tail_from) & 1) == 0) {
+          skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
+          issued_steps += static_cast<unsigned long long>(live_steps);
+        }
         // A tile without live K-blocks needs no MMA: the epilogue writes the
         // zero-accumulator result itself (the joint always has its z branch).
         if (KIND != KIND_JOINT && live_blocks == 0) continue;
@@ -633,7 +664,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     uint8_t* stage_out = s_out + ew * Tr::kSlabChunks * Tr::kStageOutBytes;
     float* bias_s = s_bias + ew * kMyChunks * 32;  // this warp's columns ch_begin*32 ..
     float* bias2_s = bias_s + EPI * kMyChunks * 32;  // KIND_JOINT: the second product's bias; KIND_UP: ln_c
-    const bool ln = KIND == KIND_UP && p.ln_c != nullptr;
+    constexpr bool ln = LN && KIND == KIND_UP;
     constexpr bool kHasRes = KIND == KIND_DOWN || KIND == KIND_JOINT;
     const bool with_res = kHasRes && p.residual != nullptr;
     const bool scatter = KIND == KIND_DOWN && p.scatter_rows > 0;
@@ -652,7 +683,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       uint4 raw = make_uint4(0u, 0u, 0u, 0u);
       if (bias_lane && bias != nullptr && t < total_tiles) {
         int mb, nc;
-        tile_coords<KIND, BN>(p, t, mb, nc);
+        work_coords<KIND, BN>(p, t, mb, nc);
         const int col = nc + ch_begin * 32 + lane * 8;
         if (col < p.N) raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(bias) + col));
       }
@@ -674,9 +705,9 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     auto load_ln = [&](int t) {
       const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
       lns_next[0] = lns_next[1] = lnc_next[0] = lnc_next[1] = z;
-      if (ln && bias_lane && t < total_tiles) {
+      if (bias_lane && t < total_tiles) {
         int mb, nc;
-        tile_coords<KIND, BN>(p, t, mb, nc);
+        work_coords<KIND, BN>(p, t, mb, nc);
         const int col = nc + ch_begin * 32 + lane * 8;
         if (col < p.N) {
           const float4* sp = reinterpret_cast<const float4*>(p.ln_s + col);
@@ -688,11 +719,11 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         }
       }
     };
-    if constexpr (KIND == KIND_UP) load_ln(unit);
+    if constexpr (ln) load_ln(unit);
 
     for (int t = unit; t < total_tiles; t += units) {
       int m_blk, n_col0;
-      tile_coords<KIND, BN>(p, t, m_blk, n_col0);
+      const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
       int live_blocks = 1, live_steps = 0;
       if constexpr (KIND != KIND_UP) count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
       const int row0 = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
@@ -703,7 +734,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const float row_mean = (ln && row_ok) ? __ldg(p.ln_mean + row) : 0.f;
       const float row_rstd = (ln && row_ok) ? __ldg(p.ln_rstd + row) : 0.f;
       const bool has_h = live_blocks > 0;                             // KIND_JOINT: the h accumulator was written
-      const int ch_end = ch_begin + kMyChunks;
+      const int ch_end = ch_begin + (half ? kMyChunks / 2 : kMyChunks);  // half: EPI == 4
       // RING > 0: the residual of chunk ch (this thread's row, 32 values) into registers.
       auto load_res = [&](int ch, uint4 (&r)[4]) {
         if constexpr (kRing && kHasRes) {
@@ -745,7 +776,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       if constexpr (KIND != KIND_HEAD) {
         __syncwarp();  // every lane is done with the previous tile's bias
         if (lane * 8 < kMyChunks * 32) {
-          if (ln) {
+          if constexpr (ln) {
             reinterpret_cast<float4*>(bias_s + lane * 8)[0] = lns_next[0];
             reinterpret_cast<float4*>(bias_s + lane * 8)[1] = lns_next[1];
             reinterpret_cast<float4*>(bias2_s + lane * 8)[0] = lnc_next[0];
@@ -758,7 +789,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         __syncwarp();
         bias_next = load_bias(p.bias, t + units);
         if constexpr (KIND == KIND_JOINT) bias2_next = load_bias(p.bias2, t + units);
-        if constexpr (KIND == KIND_UP) load_ln(t + units);
+        if constexpr (ln) load_ln(t + units);
       }
 
       if (has_acc) {

@@ -146,18 +146,19 @@ int make_out_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- launch
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0>
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr,
                 const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
   using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
-  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING>;
+  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING, LN>;
   // Setting the attribute is per function; cheap and idempotent.
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   p.m_tiles = (p.M + Tr::kTileM - 1) / Tr::kTileM;
   const int tiles = p.m_tiles * p.n_tiles;
   if (tiles == 0) return 0;
+  p.tail_from = p.work_items = tiles;
   p.status = dev->status;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -188,7 +189,19 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     }
     units = max_clusters[dev_id];
   }
-  if (tiles < units) units = tiles;
+  // The last round of the persistent grid: when it would leave at least half of the
+  // units idle, its tiles run as two half-width items each (down projection with
+  // four epilogue warps, each of which owns all columns of its rows).
+  if constexpr (KIND == KIND_DOWN && EPI == 4 && RING > 0) {
+    if (p.split_tail && tiles > units) {
+      const int rem = tiles % units;
+      if (rem > 0 && 2 * rem <= units) {
+        p.tail_from = tiles - rem;
+        p.work_items = tiles + rem;
+      }
+    }
+  }
+  if (p.work_items < units) units = p.work_items;
   cfg.gridDim = dim3(units * CG);
   e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr != nullptr ? *tr : tc, ta2 != nullptr ? *ta2 : ta,
                          tb2 != nullptr ? *tb2 : tb, p);
@@ -198,15 +211,26 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   return 0;
 }
 
-// Up-projection launch with the gate operator as a compile-time parameter.
+// Up-projection launch with the gate operator (and the folded LayerNorm) as
+// compile-time parameters.
+template <int BN, int G>
+int launch_up_gate(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
+                   bool bf16, bool ln, cudaStream_t stream, DeviceInfo* dev) {
+  constexpr int S = kUpStages, E = kUpEpiWarps, C = kUpCG, R = kUpRing;
+  if (ln)
+    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C, R, true>(ta, tb, tc, p, stream, dev)
+                : launch_gemm<KIND_UP, G, BN, S, false, E, C, R, true>(ta, tb, tc, p, stream, dev);
+  return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev)
+              : launch_gemm<KIND_UP, G, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev);
+}
+
 template <int BN>
 int launch_up(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int gate_op,
               bool bf16, cudaStream_t stream, DeviceInfo* dev) {
-  constexpr int S = kUpStages, E = kUpEpiWarps, C = kUpCG, R = kUpRing;
-#define SPMLP_UP_CASE(G)                                                                      \
-  case G:                                                                                     \
-    return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev)   \
-                : launch_gemm<KIND_UP, G, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev);
+  const bool ln = p.ln_c != nullptr;
+#define SPMLP_UP_CASE(G) \
+  case G:                \
+    return launch_up_gate<BN, G>(ta, tb, tc, p, bf16, ln, stream, dev);
   switch (gate_op) {
     SPMLP_UP_CASE(GATE_IDENTITY)
     SPMLP_UP_CASE(GATE_GELU)
@@ -335,6 +359,8 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
   const int cg = mode == SPMLP_DOWN_SKIP_FINE ? 1 : kDownCG;
   if ((rc = make_kmajor_map(&tb, w_out, d, F, BN / cg, bf16))) return rc;
+  CUtensorMap tb_half;  // half-width tail items load BN/2 columns of w_out
+  if ((rc = make_kmajor_map(&tb_half, w_out, d, F, BN / 2 / cg, bf16))) return rc;
   CUtensorMap tc, tr;
   if ((rc = make_out_map(&tc, y, T, d, bf16))) return rc;
   if (residual != nullptr && (rc = make_out_map(&tr, residual, T, d, bf16))) return rc;
@@ -350,6 +376,7 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   p.bits_words = spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
+  p.split_tail = 1;
   if (slots != nullptr) {
     p.scatter_rows = static_cast<int>(T / world);
     for (int j = 0; j < world; ++j) p.scatter_out[j] = slots[j];
@@ -358,11 +385,11 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps, RF = kDownFineRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
   if (mode == SPMLP_DOWN_SKIP_FINE) {
-    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp);
-    return launch_gemm<KIND_DOWN, 0, BN, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp);
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
+    return launch_gemm<KIND_DOWN, 0, BN, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
   }
-  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp);
-  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp);
+  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
+  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
 }
 
 int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w2, const void* b2, const void* wo,
