@@ -272,9 +272,24 @@ int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, 
                     float value, void* stream);
 
 /* Status word of `device` written by kernels that gave up on a bounded wait
- * (0 = none).  Reading synchronises that device.  clear resets it to 0. */
+ * (0 = none; the first code recorded stays until cleared; once it is set, later
+ * waits give up at once so a failed launch unwinds quickly).  Reading
+ * synchronises that device.  clear resets it to 0. */
+#define SPMLP_STATUS_OK 0
+#define SPMLP_STATUS_TIMEOUT_PRODUCER 1 /* TMA warp: no free pipeline stage          */
+#define SPMLP_STATUS_TIMEOUT_MMA 2      /* MMA warp: no loaded stage / free TMEM     */
+#define SPMLP_STATUS_TIMEOUT_EPILOGUE 3 /* epilogue: no finished accumulator         */
+#define SPMLP_STATUS_TIMEOUT_DRAIN 4    /* teardown: in-flight copies / MMAs pending */
+#define SPMLP_STATUS_TIMEOUT_PROBE 5    /* spmlp_selftest_wait                       */
 int spmlp_device_status(int device, int* status_out);
 int spmlp_clear_device_status(int device);
+
+/* Self-test of failure detection (no counterpart in the reference): one kernel
+ * waits, with the bounded wait every kernel here uses, on a barrier that nothing
+ * completes.  After about 2 s it gives up, records SPMLP_STATUS_TIMEOUT_PROBE in
+ * the status word and returns; the context stays usable.  Nothing faults or
+ * traps.  Clear the status word first: a set word makes the wait give up at once. */
+int spmlp_selftest_wait(void* stream);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* spmlp_last_error(void);

@@ -24,6 +24,7 @@ enum DeviceStatus : int {
   kDevTimeoutMma = 2,        // MMA warp gave up waiting for a loaded stage / free accumulator
   kDevTimeoutEpilogue = 3,   // epilogue gave up waiting for a finished accumulator
   kDevTimeoutDrain = 4,      // teardown gave up waiting for in-flight copies / MMAs
+  kDevTimeoutProbe = 5,      // spmlp_selftest_wait: the deliberate wait that nothing completes
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -444,6 +444,19 @@ int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w
   return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
 }
 
+// A bounded wait on an mbarrier that nothing arrives on: the same wait helper every
+// kernel uses gives up after SPMLP_WAIT_NS, records kDevTimeoutProbe in the status
+// word and the kernel returns normally.
+__global__ void wait_probe_kernel(int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, status, kDevTimeoutProbe);
+}
+
 int row_stats_impl(const void* x, float* mean, float* rstd, int64_t T, int d, int dtype, float eps,
                    cudaStream_t stream) {
   int rc;
@@ -924,6 +937,16 @@ int spmlp_head_sparse(const void* x, const uint32_t* support, const void* w_voca
 int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype, float value,
                     void* stream) {
   return head_fill_impl(logits, tiles, n_tiles, T, V, dtype, value, static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_selftest_wait(void* stream) {
+  DeviceInfo* dev = nullptr;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "wait_probe_kernel launch");
+  return 0;
 }
 
 int spmlp_device_status(int device, int* status_out) {

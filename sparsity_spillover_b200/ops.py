@@ -475,6 +475,13 @@ def device_status(device: int | None = None) -> int:
     return out.value
 
 
+def selftest_wait(device: int | None = None) -> None:
+    """Launch the bounded-wait self-test (see include/spmlp.h) on the current stream."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    with torch.cuda.device(dev):
+        _lib.call("spmlp_selftest_wait", _stream(dev))
+
+
 def clear_device_status(device: int | None = None) -> None:
     dev = torch.cuda.current_device() if device is None else int(device)
     _lib.call("spmlp_clear_device_status", dev)

@@ -335,3 +335,27 @@ def test_persisted_bitmap_drives_the_down_projection_identically(tmp_path, encod
     y_a = ops.down_sparse(h, bits, w, None, stats=st_a)
     y_b = ops.down_sparse(h, loaded, w, None, stats=st_b)
     assert torch.equal(y_a, y_b) and torch.equal(st_a, st_b) and int(st_a[1]) > 0
+
+
+def test_bounded_wait_times_out_reports_and_leaves_the_context_usable():
+    """Failure detection without a fault: a wait that nothing completes gives up after
+    ~2 s, the status word says which wait, and the GPU keeps working."""
+    import time
+
+    from sparsity_spillover_b200 import ops
+
+    ops.clear_device_status()
+    assert ops.device_status() == 0
+    start = time.perf_counter()
+    ops.selftest_wait()
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - start
+    assert ops.device_status() == 5  # SPMLP_STATUS_TIMEOUT_PROBE
+    assert 1.0 < elapsed < 30.0
+    ops.clear_device_status()
+    # The context still runs the kernels, with correct results.
+    h = torch.zeros(64, 256, dtype=torch.float16, device="cuda")
+    h[17, 70] = 1.0
+    bits = ops.tile_bits_from_h(h)
+    assert bits.cpu().tolist() == [0, 2, 0, 0]
+    assert ops.device_status() == 0
