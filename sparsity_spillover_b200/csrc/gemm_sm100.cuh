@@ -482,6 +482,10 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above may overlap the tail of the previous kernel in the stream;
+  // nothing below reads global memory before that kernel has completed.
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)

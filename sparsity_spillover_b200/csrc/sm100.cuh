@@ -204,6 +204,14 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// Programmatic dependent launch (launches with cudaLaunchAttributeProgrammatic-
+// StreamSerialization): wait until the previous kernel in the stream has completed
+// and its writes are visible; a no-op for a launch without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel in the stream begin launching (its CTAs still wait in
+// grid_dependency_wait before touching this kernel's outputs).
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

@@ -44,6 +44,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 constexpr int kMaxDevices = 64;
+constexpr int kProgrammaticLaunch = 1;  // GEMM launches overlap the previous kernel's tail
 
 // Tile configuration of the up-projection: pipeline stages, epilogue warps,
 // CTAs per tile, output ring slots per epilogue warp (0 = whole-tile slab).
@@ -161,28 +162,36 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   p.tail_from = p.work_items = tiles;
   p.status = dev->status;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.blockDim = dim3(Tr::kThreads);
   cfg.dynamicSmemBytes = Tr::kSmemBytes;
   cfg.stream = stream;
+  // Programmatic dependent launch: this kernel's set-up may overlap the previous
+  // kernel's tail (the kernel waits with griddepcontrol.wait before reading inputs).
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   int units = dev->sm_count;  // persistent: one CTA (or CTA pair) per SM (pair)
   if constexpr (CG > 1) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(cluster size)");
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CG;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = CG;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
     // Clusters that can be resident at once, queried once per device for this kernel.
     static int max_clusters[kMaxDevices] = {};
     int dev_id = 0;
     cudaGetDevice(&dev_id);
     if (max_clusters[dev_id] == 0) {
-      cfg.gridDim = dim3(dev->sm_count);
+      cudaLaunchConfig_t query = cfg;  // the cluster shape alone decides residency
+      query.gridDim = dim3(dev->sm_count);
+      query.attrs = &attr[1];
+      query.numAttrs = 1;
       int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&n, kernel, &query);
       if (e != cudaSuccess || n <= 0) return cuda_fail(e == cudaSuccess ? cudaErrorInvalidConfiguration : e,
                                                        "cudaOccupancyMaxActiveClusters");
       max_clusters[dev_id] = n;
