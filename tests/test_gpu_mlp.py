@@ -359,3 +359,28 @@ def test_bounded_wait_times_out_reports_and_leaves_the_context_usable():
     bits = ops.tile_bits_from_h(h)
     assert bits.cpu().tolist() == [0, 2, 0, 0]
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("skip", [True, "fine"])
+def test_last_round_split_tiles_match_the_oracle(skip):
+    """At T=32768, d=512 the persistent grid's last round (coarse: 34 of 256 tiles on
+    74 CTA pairs; fine: 68 of 512 on 148 CTAs) runs as half-width items: the final
+    token blocks, both column halves, and the skip counts match the oracle."""
+    from sparsity_spillover_b200 import ops, workloads
+
+    t, d, f = 32768, 512, 2048
+    h, _ = workloads.tile_structured_h(t, f, 0.2, seed=17, device=DEV, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(18)
+    w_out = (torch.randn(d, f, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    b_out = (torch.randn(d, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    r = torch.randn(t, d, generator=g).to(torch.bfloat16).to(DEV)
+    bits = ops.tile_bits_from_h(h)
+    stats = torch.zeros(2, dtype=torch.int64, device=DEV)
+    y = ops.down_sparse(h, bits, w_out, b_out, r, skip=skip, stats=stats)
+    torch.cuda.synchronize()
+    tail = slice(t - 4096, t)
+    h_c = h.cpu()
+    y_ref = omlp.down_from_h(h_c[tail], w_out.cpu(), b_out.cpu(), residual=r.cpu()[tail], dtype=torch.bfloat16)
+    assert omlp.max_rel_error(y.cpu()[tail], y_ref) <= TOL[torch.bfloat16]
+    issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=d // 256, m_tile=ops.down_tile_tokens(skip))
+    assert stats.cpu().tolist() == [issued, skipped]
