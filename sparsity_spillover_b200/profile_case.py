@@ -1,14 +1,15 @@
 """Run a few launches of one kernel on a benchmark config, for profilers (ncu).
 
     python -m sparsity_spillover_b200.profile_case --case mlp  [--tokens 32768] [--iters 3]
-    python -m sparsity_spillover_b200.profile_case --case tile [--p 0.1]
+    python -m sparsity_spillover_b200.profile_case --case tile [--p 0.1] [--skip fine]
     python -m sparsity_spillover_b200.profile_case --case head [--d 128] [--frac 0.1]
     python -m sparsity_spillover_b200.profile_case --case joint [--tokens 32768]
 
 * ``mlp``  one cfg1 layer (d=512, F=2048, fp16, one-sided gate at 10% density):
            up_gate then down_sparse with the residual, ``iters`` times.
 * ``tile`` cfg2: a tile-structured bf16 h (64x64 tiles live with probability p),
-           its bitmap, and the tile-skipping down_sparse (d=512, F=2048).
+           its bitmap, and the tile-skipping down_sparse (d=512, F=2048) in the
+           ``--skip`` mode (coarse: 256-token pair tiles, fine: 128-token tiles).
 * ``head`` cfg4: the N-gated vocabulary head on Zipf-chosen 128-column tiles.
 * ``joint`` the joint consumer on a cfg1 layer: up_gate (identity, then gated) once,
            then the joint kernel ``iters`` times (h at 10% density, z ~ N(0,1)).
@@ -32,6 +33,7 @@ def main() -> None:
     ap.add_argument("--p", type=float, default=0.1)
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--frac", type=float, default=0.1)
+    ap.add_argument("--skip", choices=["coarse", "fine"], default="coarse")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     with torch.inference_mode():
@@ -65,7 +67,7 @@ def main() -> None:
             y = torch.empty(args.tokens, 512, dtype=torch.bfloat16, device=dev)
             for _ in range(args.iters):
                 ops.tile_bits_from_h(h, bits)
-                ops.down_sparse(h, bits, w, None, y=y)
+                ops.down_sparse(h, bits, w, None, skip=args.skip, y=y)
         else:
             x, w = workloads.head_inputs(args.tokens, args.d, seed=4, device=dev)
             tiles = torch.from_numpy(workloads.zipf_active_tiles(workloads.VOCAB // 128, args.frac, 5)).to(dev)
