@@ -56,6 +56,8 @@ constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
 constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
 constexpr int kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
+// Vocabulary head: 128 x 128 tiles on single CTAs.
+constexpr int kHeadStages = 4, kHeadEpiWarps = 8, kHeadRing = 2;
 // Joint consumer: 256 output columns per tile, so that h is read by only d/256
 // column tiles; the tile's two accumulators then fill TMEM's 512 columns and are
 // single-buffered (measured on cfg1: 96 us against 121 us for double-buffered
@@ -636,8 +638,11 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   p.bits_words = spmlp_head_support_words(d);
   p.skip = gate_axis == SPMLP_HEAD_GATE_K ? 1 : 0;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
-  if (bf16) return launch_gemm<KIND_HEAD, 0, BN, 4, true, 4, 1>(ta, tb, tc, p, stream, dev);
-  return launch_gemm<KIND_HEAD, 0, BN, 4, false, 4, 1>(ta, tb, tc, p, stream, dev);
+  // Eight epilogue warps (two 32-column chunks each) and a two-slot output ring:
+  // the logit stores, not the MMAs, bound the head at d = 128.
+  constexpr int S = kHeadStages, E = kHeadEpiWarps, R = kHeadRing;
+  if (bf16) return launch_gemm<KIND_HEAD, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev);
+  return launch_gemm<KIND_HEAD, 0, BN, S, false, E, 1, R>(ta, tb, tc, p, stream, dev);
 }
 
 int head_fill_impl(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype, float value,
