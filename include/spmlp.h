@@ -167,6 +167,15 @@ int spmlp_down_scatter(const void* h, const uint32_t* tile_bits, const void* w_o
                        int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, void* stream);
 int spmlp_reduce_broadcast(const void* recv, int world, int64_t rows, int d, const void* b_out,
                            const void* residual, void* const* targets, int n_targets, int dtype, void* stream);
+/* Barrier between the ranks of the fused d_ff split over NVLink peer memory,
+ * ordered on `stream`: this rank stores `epoch` into peer_slots[j] (its slot in
+ * rank j's int64 flag array, [world]) after a system-scope fence, then waits until
+ * local_flags[j] >= epoch for every j.  epoch must grow from call to call (flags
+ * start at 0).  Each wait gives up after about 2 s with SPMLP_STATUS_TIMEOUT_PEER
+ * in the status word; nothing faults.  One rank per GPU: ranks sharing a GPU can
+ * wait on each other forever, so that is not supported. */
+int spmlp_peer_barrier(long long* const* peer_slots, const long long* local_flags, int world, long long epoch,
+                       void* stream);
 
 /* Joint consumer: the MLP's down projection and the attention output
  * projection of one GPT-NeoX layer, summed with its parallel residual, in one
@@ -281,6 +290,7 @@ int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, 
 #define SPMLP_STATUS_TIMEOUT_EPILOGUE 3 /* epilogue: no finished accumulator         */
 #define SPMLP_STATUS_TIMEOUT_DRAIN 4    /* teardown: in-flight copies / MMAs pending */
 #define SPMLP_STATUS_TIMEOUT_PROBE 5    /* spmlp_selftest_wait                       */
+#define SPMLP_STATUS_TIMEOUT_PEER 6     /* spmlp_peer_barrier: a peer did not signal */
 int spmlp_device_status(int device, int* status_out);
 int spmlp_clear_device_status(int device);
 

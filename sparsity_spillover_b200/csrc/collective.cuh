@@ -57,4 +57,32 @@ __global__ void __launch_bounds__(256) reduce_broadcast_kernel(const uint16_t* _
   __threadfence_system();  // peer stores are performed before the kernel completes
 }
 
+struct PeerFlags {
+  long long* dst[kMaxRanks];  // this rank's slot in each rank's flag array (peer memory)
+};
+
+// Barrier over NVLink peer memory: thread j stores `epoch` into this rank's slot of
+// rank j's flags (after a system-scope fence, so this rank's earlier peer stores
+// are visible first), then waits until rank j's epoch has arrived in `local`.
+// Every wait is bounded: after SPMLP_WAIT_NS it records kDevTimeoutPeer and gives up.
+__global__ void peer_barrier_kernel(PeerFlags peers, const long long* local, int world, long long epoch,
+                                    int* status) {
+  const int j = threadIdx.x;
+  if (j >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(peers.dst[j]), "l"(epoch) : "memory");
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    long long seen;
+    asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(seen) : "l"(local + j) : "memory");
+    if (seen >= epoch) break;
+    if (*reinterpret_cast<volatile int*>(status) != kDevOk) break;  // another wait already failed
+    if (global_timer_ns() - start > SPMLP_WAIT_NS) {
+      atomicCAS(status, kDevOk, kDevTimeoutPeer);
+      break;
+    }
+    __nanosleep(100);
+  }
+}
+
 }  // namespace spmlp

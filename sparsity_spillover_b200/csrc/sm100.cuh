@@ -25,6 +25,7 @@ enum DeviceStatus : int {
   kDevTimeoutEpilogue = 3,   // epilogue gave up waiting for a finished accumulator
   kDevTimeoutDrain = 4,      // teardown gave up waiting for in-flight copies / MMAs
   kDevTimeoutProbe = 5,      // spmlp_selftest_wait: the deliberate wait that nothing completes
+  kDevTimeoutPeer = 6,       // spmlp_peer_barrier: a peer rank did not signal in time
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -953,6 +953,27 @@ int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, 
   return head_fill_impl(logits, tiles, n_tiles, T, V, dtype, value, static_cast<cudaStream_t>(stream));
 }
 
+int spmlp_peer_barrier(long long* const* peer_slots, const long long* local_flags, int world, long long epoch,
+                       void* stream) {
+  if (!peer_slots || !local_flags) return fail(SPMLP_EINVAL, "peer_slots and local_flags must be non-null");
+  if (world < 1 || world > kMaxRanks) return fail(SPMLP_EINVAL, "world=%d must be in [1, %d]", world, kMaxRanks);
+  if (epoch < 1) return fail(SPMLP_EINVAL, "epoch must be positive and increase from call to call");
+  PeerFlags pf{};
+  for (int j = 0; j < world; ++j) {
+    if (!peer_slots[j] || (reinterpret_cast<uintptr_t>(peer_slots[j]) & 7u))
+      return fail(SPMLP_EALIGN, "peer slot %d must be non-null and 8-byte aligned", j);
+    pf.dst[j] = peer_slots[j];
+  }
+  if (reinterpret_cast<uintptr_t>(local_flags) & 7u) return fail(SPMLP_EALIGN, "local_flags must be 8-byte aligned");
+  DeviceInfo* dev = nullptr;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pf, local_flags, world, epoch, dev->status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "peer_barrier_kernel launch");
+  return 0;
+}
+
 int spmlp_selftest_wait(void* stream) {
   DeviceInfo* dev = nullptr;
   int rc = current_device_info(&dev);

@@ -160,9 +160,11 @@ class FusedDffSplit:
     receive buffer; a one-element all-reduce orders it before every rank's
     reduction, which sums its block's slots in fp32, adds b_out and the residual
     (rounding like ``DffSplitMLP.forward``) and writes the block into every rank's X;
-    a second one-element all-reduce orders that before the next layer.  X and the
-    receive buffers are torch symmetric-memory tensors, so peers' addresses come
-    from its rendezvous; tokens per rank must be a multiple of 256.
+    a second barrier orders that before the next layer.  The barriers are
+    ``spmlp_peer_barrier`` (epoch flags stored into peers' memory over NVLink, bounded
+    waits); NCCL is used only once, to order the flags' initialisation.  X, the receive
+    buffers and the flags are torch symmetric-memory tensors, so peers' addresses come
+    from its rendezvous; tokens per rank must be a multiple of 256; one rank per GPU.
     """
 
     def __init__(self, layers: list[DffSplitMLP], tokens: int, *, skip: bool | str = True):
@@ -193,13 +195,24 @@ class FusedDffSplit:
         # My slot in each rank's receive buffer, and my token block in each rank's X.
         self.slots = [int(hr.buffer_ptrs[j]) + self.rank * block for j in range(self.world)]
         self.targets = [int(hx.buffer_ptrs[j]) + self.rank * block for j in range(self.world)]
-        self._handles = (hx, hr)
         self.h = torch.empty((tokens, self.f), dtype=self.dtype, device=self.device)
         self.bits = torch.empty((ops.tile_bits_size(tokens, self.f),), dtype=torch.int32, device=self.device)
-        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.flags = symm_mem.empty((self.world,), dtype=torch.int64, device=self.device)
+        self.flags.zero_()
+        hf = symm_mem.rendezvous(self.flags, group)
+        self.flag_slots = [int(hf.buffer_ptrs[j]) + self.rank * 8 for j in range(self.world)]
+        self._handles = (hx, hr, hf)
+        self.epoch = 0
+        torch.cuda.synchronize(self.device)
+        one = torch.zeros(1, dtype=torch.int32, device=self.device)
+        dist.all_reduce(one, group=self.group)  # every rank's flags are zero before the first barrier
+        torch.cuda.synchronize(self.device)
 
     def _barrier(self) -> None:
-        dist.all_reduce(self._flag, group=self.group)
+        from . import ops
+
+        self.epoch += 1
+        ops.peer_barrier(self.flag_slots, self.flags, self.epoch)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """x [T, d] (the same on every rank) -> this rank's [T/w, d] block of the last

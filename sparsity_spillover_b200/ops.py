@@ -316,6 +316,16 @@ def reduce_broadcast(recv: torch.Tensor, b_out: torch.Tensor | None, residual: t
     del keep
 
 
+def peer_barrier(peer_slots: list[int], local_flags: torch.Tensor, epoch: int) -> None:
+    """Device-side barrier of the fused d_ff split over NVLink (see include/spmlp.h)."""
+    device = local_flags.device
+    _check("local_flags", local_flags, torch.int64, device, (len(peer_slots),))
+    arr, keep = _pointer_array([int(v) for v in peer_slots])
+    with torch.cuda.device(device):
+        _lib.call("spmlp_peer_barrier", arr, _ptr(local_flags), len(peer_slots), int(epoch), _stream(device))
+    del keep
+
+
 def joint(h: torch.Tensor, bits: torch.Tensor | None, z: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor | None,
           wo: torch.Tensor, bo: torch.Tensor | None, residual: torch.Tensor | None = None, *,
           skip: bool | str = True, out: torch.Tensor | None = None,

@@ -64,7 +64,20 @@ def _worker(rank, world, port, queue):
         same_again = bool(torch.equal(y_again, y_fused)) and bool(torch.equal(fused.x, full_x))
         rows_ok = omlp.max_rel_error(full_x.float().cpu(), ref.float().cpu())  # every block reached every rank
         torch.cuda.synchronize(dev)
-        queue.put((rank, err, same, ops.device_status(rank), err_fused, same_again, rows_ok))
+        status = ops.device_status(rank)
+        # Failure detection without a fault: rank 0 waits for an epoch that rank 1 never
+        # signals; the bounded wait gives up, the status word says so, the GPU keeps working.
+        timeout_status, usable = 6, True
+        if rank == 0:
+            ops.clear_device_status(rank)
+            ops.peer_barrier(fused.flag_slots, fused.flags, fused.epoch + 1000)
+            torch.cuda.synchronize(dev)
+            timeout_status = ops.device_status(rank)
+            ops.clear_device_status(rank)
+            probe = torch.zeros(64, 128, dtype=torch.float16, device=dev)
+            probe[5, 70] = 1.0
+            usable = ops.tile_bits_from_h(probe).cpu().tolist() == [2, 0, 0, 0]
+        queue.put((rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable))
     finally:
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
@@ -83,10 +96,11 @@ def test_dff_split_over_nccl_and_token_shards():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, err, same, status, err_fused, same_again, rows_ok in results:
+    for rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable in results:
         assert err <= 2e-2, (rank, err)  # fp16 partials summed by NCCL, then bias and residual rounding
         assert same
         assert status == 0
         assert err_fused <= 2e-2, (rank, err_fused)  # fp16 partials summed in fp32
         assert same_again
         assert rows_ok <= 2e-2, (rank, rows_ok)
+        assert timeout_status == 6 and usable  # SPMLP_STATUS_TIMEOUT_PEER

@@ -84,6 +84,15 @@ def test_joint_and_gate_argument_errors_without_a_gpu(lib):
     assert rc == -1 and b"kappa" in lib.spmlp_last_error()
     rc = lib.spmlp_gate(16, 1024, None, 64, 512, 0, 2, k, None)
     assert rc == -1 and b"overlap" in lib.spmlp_last_error()
+    # peer_slots, local_flags, world, epoch, stream
+    slots = (ctypes.c_void_p * 2)(16, 24)
+    rc = lib.spmlp_peer_barrier(ctypes.cast(slots, ctypes.POINTER(ctypes.c_void_p)), 16, 9, 1, None)
+    assert rc == -1 and b"world" in lib.spmlp_last_error()
+    rc = lib.spmlp_peer_barrier(ctypes.cast(slots, ctypes.POINTER(ctypes.c_void_p)), 16, 2, 0, None)
+    assert rc == -1 and b"epoch" in lib.spmlp_last_error()
+    bad = (ctypes.c_void_p * 2)(16, 20)
+    rc = lib.spmlp_peer_barrier(ctypes.cast(bad, ctypes.POINTER(ctypes.c_void_p)), 16, 2, 1, None)
+    assert rc == -3
 
 
 def test_joint_consumer_reads_the_reference_gates():
