@@ -199,12 +199,12 @@ class Stack:
         return self.xs[-1]
 
 
-def dense_reference_step(stack: Stack):
+def dense_reference_step(stack: Stack, x=None):
     """The same 6-layer forward as stock PyTorch runs it on CUDA: cuBLAS Linear, masked_fill gate,
     residual add (the reference's own GPU path for the block, without custom kernels)."""
     import torch
 
-    x = stack.x0
+    x = stack.x0 if x is None else x
     for layer, gate in zip(stack.layers, stack.gates):
         z = torch.nn.functional.linear(x, layer.w_in, layer.b_in)
         if gate["operator"] == "one_sided_threshold":
@@ -250,6 +250,38 @@ def density_sweep(device, densities=(1.0, 0.5, 0.25, 0.1, 0.05), steps=5) -> lis
     for r in rows:
         r["speedup_vs_ours_at_100pct"] = r["tokens_per_s"] / base
     return rows
+
+
+def paired_cfg1(device, passes: int = 3, n_inputs: int = 4, warmups: int = 2) -> dict:
+    """cfg1 under the reference's paired, rotating-input latency protocol
+    (runs/025-…/measurement.py:26-97): four seeded input batches, every (pass, input)
+    block running {stock PyTorch at rho = 0.1, ours at rho = 1, ours at rho = 0.1} in a
+    shuffled order, eager calls, synchronised host latency as the primary figure and
+    the paired geometric-mean speed-up over stock PyTorch."""
+    from sparsity_spillover_b200 import measurement, workloads
+
+    stacks = {"ours_rho10": Stack(device, 0, DENSITY), "ours_rho100": Stack(device, 0, 1.0)}
+    cfg = stacks["ours_rho10"].cfg
+    inputs = [workloads.make_input(cfg, device, token_offset=1000 + i) for i in range(n_inputs)]
+    modes = ["dense_pytorch", "ours_rho100", "ours_rho10"]
+    current = {"mode": modes[0]}
+
+    def set_mode(mode):
+        current["mode"] = mode
+
+    def forward(x):
+        if current["mode"] == "dense_pytorch":
+            return dense_reference_step(stacks["ours_rho10"], x)
+        st = stacks[current["mode"]]
+        st.xs[0] = x
+        return st.step()
+
+    samples = measurement.paired_timing(forward, set_mode, inputs, modes=modes, passes=passes, warmups=warmups,
+                                        seed=2026)
+    return {"protocol": f"paired rotating inputs: {n_inputs} inputs x {passes} passes, shuffled mode order, "
+                        f"{warmups} warm-ups per mode, eager calls, seed 2026",
+            "density_measured": {k: round(v.density, 4) for k, v in stacks.items()},
+            "summary": measurement.timing_summary(samples, reference="dense_pytorch", tokens_per_call=cfg.tokens)}
 
 
 def tile_structured(device, steps=10) -> list[dict]:
@@ -676,6 +708,7 @@ def run_ours(args):
 
         with torch.inference_mode():
             line["density_sweep"] = _extra(density_sweep, device)
+            line["paired_protocol_cfg1"] = _extra(paired_cfg1, device)
             line["tile_structured_cfg2"] = _extra(tile_structured, device)
             line["pythia410m_cfg3"] = _extra(cfg3_410m, device)
             line["vocab_head_cfg4"] = _extra(head_bench, device)

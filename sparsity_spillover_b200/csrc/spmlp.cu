@@ -55,7 +55,7 @@ constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
 // goes to six operand stages (the loads of h are the bound).
 constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
-constexpr int kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
+constexpr int kDownFineBN = 256, kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
 // Vocabulary head: 128 x 128 tiles on single CTAs.
 constexpr int kHeadStages = 4, kHeadEpiWarps = 8, kHeadRing = 2;
 // Joint consumer: 256 output columns per tile, so that h is read by only d/256
@@ -365,13 +365,15 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   DeviceInfo* dev = nullptr;
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
-  constexpr int BN = 256;
+  constexpr int BN = 256, BNF = kDownFineBN;
+  const bool fine = mode == SPMLP_DOWN_SKIP_FINE;
+  const int bn = fine ? BNF : BN;
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
-  const int cg = mode == SPMLP_DOWN_SKIP_FINE ? 1 : kDownCG;
-  if ((rc = make_kmajor_map(&tb, w_out, d, F, BN / cg, bf16))) return rc;
-  CUtensorMap tb_half;  // half-width tail items load BN/2 columns of w_out
-  if ((rc = make_kmajor_map(&tb_half, w_out, d, F, BN / 2 / cg, bf16))) return rc;
+  const int cg = fine ? 1 : kDownCG;
+  if ((rc = make_kmajor_map(&tb, w_out, d, F, bn / cg, bf16))) return rc;
+  CUtensorMap tb_half;  // half-width tail items load bn/2 columns of w_out
+  if ((rc = make_kmajor_map(&tb_half, w_out, d, F, bn / 2 / cg, bf16))) return rc;
   CUtensorMap tc, tr;
   if ((rc = make_out_map(&tc, y, T, d, bf16))) return rc;
   if (residual != nullptr && (rc = make_out_map(&tr, residual, T, d, bf16))) return rc;
@@ -379,7 +381,7 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   p.M = static_cast<int>(T);
   p.N = d;
   p.K = F;
-  p.n_tiles = (d + BN - 1) / BN;
+  p.n_tiles = (d + bn - 1) / bn;
   p.bias = b_out;
   p.out = y;
   p.residual = residual;
@@ -395,9 +397,9 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   constexpr int S = kDownStages, E = kDownEpiWarps, C = kDownCG, R = kDownRing;
   constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps, RF = kDownFineRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
-  if (mode == SPMLP_DOWN_SKIP_FINE) {
-    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
-    return launch_gemm<KIND_DOWN, 0, BN, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
+  if (fine) {
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BNF, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
+    return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
   }
   if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
   return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);

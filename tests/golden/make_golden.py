@@ -16,6 +16,8 @@ Every fixture is produced by executing the reference's modules, never the oracle
 * counts.npz     runs/042-…/tile_oracle.py counts() on structured tensors.
 * joint.npz      runs/042-…/controls.py NativeJoint in bf16 with exactly representable values.
 * head.npz       runs/068-…/inference/head.py pack_weight; diagnostics.py counts() certificates.
+* measurement.npz runs/025-…/measurement.py paired_schedule (several counts, passes, mode lists and
+                 seeds) and timing_summary on fixed synthetic samples.
 """
 from __future__ import annotations
 
@@ -32,6 +34,7 @@ HERE = Path(__file__).resolve().parent
 R042 = "runs/042-2026-09-20-pythia70m-sparse-scale"
 R063 = "runs/063-2026-10-07-pythia14m-tile-specialized-kernel"
 R068 = "runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference"
+R025 = "runs/025-2026-09-05-pythia-agentic-sparse-kernel-search"
 
 
 def load(name: str, path: Path):
@@ -180,15 +183,45 @@ def head(ref: Path) -> dict:
     return out
 
 
+# (count, passes, modes, seed) cases of the paired schedule
+SCHEDULE_CASES = [(1, 1, ("native",), 0), (3, 2, ("native", "fused", "sparse"), 7),
+                  (4, 3, ("dense_pytorch", "ours_rho100", "ours_rho10"), 2026), (5, 2, ("a", "b"), 123456789)]
+
+
+def measurement(ref: Path) -> dict:
+    meas = load("golden_measurement", ref / R025 / "measurement.py")
+    out = {}
+    for i, (count, passes, modes, seed) in enumerate(SCHEDULE_CASES):
+        rows = meas.paired_schedule(count, passes, list(modes), seed)
+        out[f"schedule{i}"] = np.array([[rep, idx] + [modes.index(m) for m in order] for rep, idx, order in rows])
+    # timing_summary on fixed samples: 3 modes x 2 passes x 3 inputs, host_ms from a fixed rule
+    modes = ("native", "a", "b")
+    samples = []
+    for rep in range(2):
+        for idx in range(3):
+            for j, mode in enumerate(modes):
+                samples.append({"repeat": rep, "input_index": idx, "mode": mode,
+                                "host_ms": 1.0 + 0.25 * j + 0.125 * idx + 0.0625 * rep * (j + 1), "cuda_ms": None})
+    summary = meas.timing_summary(samples, reference="native")
+    out["summary_host_ms"] = np.array([s["host_ms"] for s in samples])
+    out["summary_median"] = np.array([summary[m]["median_host_ms"] for m in modes])
+    out["summary_geomean"] = np.array([summary[m]["paired_geomean_speedup"] for m in modes])
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", nargs="*", help="fixture names to regenerate (default: all)")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref / "src"))
     torch.set_num_threads(1)
     for name, fn in (("gates", lambda: gates(ref)), ("mlp_cfg0", mlp_cfg0), ("counts", lambda: counts(ref)),
-                     ("joint", lambda: joint(ref)), ("head", lambda: head(ref))):
+                     ("joint", lambda: joint(ref)), ("head", lambda: head(ref)),
+                     ("measurement", lambda: measurement(ref))):
+        if args.only and name not in args.only:
+            continue
         arrays = fn()
         np.savez_compressed(HERE / f"{name}.npz", **arrays)
         print(name, sum(a.nbytes for a in arrays.values()), "bytes")
