@@ -674,6 +674,12 @@ def run_ours(args):
     traffic = NCU_TRAFFIC_BYTES.get(dom)
     # density-scaled algorithmic work of the whole step (f(ormula): L (2Tdf + 2Tdf rho))
     ideal_flop = nl * (2.0 * t * d * f + 2.0 * t * d * f * DENSITY)
+    # the matching bytes (2-byte activations and weights): x, W_in, b_in, h written, the live
+    # fraction rho_t of h read back, W_out, b_out, y, and the 16x64 bitmap (one bit per 1024 values)
+    rho_t = stats[0] / max(1, stats[0] + stats[1])
+    ideal_bytes = nl * 2.0 * (t * d + d * f + f + t * f + rho_t * t * f + f * d + d + t * d) + nl * t * f / 8192.0
+    t_flop_s, t_byte_s = ideal_flop / (peak_tf * 1e12), ideal_bytes / (p["hbm_gbs"] * 1e9)
+    bound_s = max(t_flop_s, t_byte_s)
     value = world * t / t_step
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -689,14 +695,20 @@ def run_ours(args):
                      "up_gate_us": t_up * 1e6, "down_sparse_us": t_dn * 1e6},
         "density_scaled_roofline": {"algorithmic_tflop_per_step": ideal_flop / 1e12,
                                     "achieved_tflops": ideal_flop / t_step / 1e12,
-                                    "frac": ideal_flop / t_step / 1e12 / peak_tf},
+                                    "frac": ideal_flop / t_step / 1e12 / peak_tf,
+                                    "live_k16_fraction": rho_t, "algorithmic_gb_per_step": ideal_bytes / 1e9,
+                                    "achieved_gbs": ideal_bytes / t_step / 1e9,
+                                    "frac_hbm": ideal_bytes / t_step / 1e9 / p["hbm_gbs"],
+                                    "time_bound_us": bound_s * 1e6, "bound": "tensor" if t_flop_s >= t_byte_s else "hbm",
+                                    "step_over_bound": t_step / bound_s},
         "skip_stats_calibration": {"issued_k16": stats[0], "skipped_k16": stats[1]},
         "dense_pytorch_cuda": {"tokens_per_s": t / dense_ref_t, "speedup": dense_ref_t / (t_step)},
         "e2e": {"value": world * t / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": t * d * 2,
                 "d2h_bytes_per_step": t * d * 2, "pipelining": "batches: H2D(i+1) and D2H(i-1) overlap compute(i)",
                 "matches_device_forward": e2e_ok, "ms_per_step": t_e2e * 1e3},
-        "gpu_launches": args.steps * nl * 2,
-        "execution": "value: CUDA-graph replay of the 6-layer step (12 kernels + 6 bitmap memsets per step); "
+        "gpu_launches": args.steps * nl * 3,
+        "execution": "value: CUDA-graph replay of the 6-layer step (18 kernels per step: bitmap clear, up_gate, "
+                     "down_sparse per layer, chained by programmatic dependent launch); "
                      "roofline: eager steps with per-kernel CUDA events",
         "clocks": clocks,
         "device_status": status,

@@ -674,9 +674,9 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     const bool scatter = KIND == KIND_DOWN && p.scatter_rows > 0;
     int ring_slot = 0;  // RING > 0: next slot of this warp's ring (carries across tiles)
     // The accumulator-release barriers live in the leader CTA.
-    uint32_t acc_empty_addr[2];
-    for (int i = 0; i < 2; ++i)
-      acc_empty_addr[i] = (CG == 1) ? smem_u32(&acc_empty[i]) : mapa_shared(smem_u32(&acc_empty[i]), 0);
+    // The two barriers are adjacent, so the leader's copy of barrier i is at base + 8 i
+    // (computed rather than indexed from an array, which would live in local memory).
+    const uint32_t acc_empty_leader = (CG == 1) ? smem_u32(&acc_empty[0]) : mapa_shared(smem_u32(&acc_empty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0, res_phase = 0;
     const uint32_t k2 = DType<BF16>::pack_rn(p.kappa, p.kappa);  // kappa in both halves (exact: pre-rounded)
@@ -818,7 +818,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           if constexpr (CG == 1)
             mbar_arrive(&acc_empty[acc]);
           else
-            mbar_arrive_cluster(acc_empty_addr[acc]);
+            mbar_arrive_cluster(acc_empty_leader + 8u * static_cast<uint32_t>(acc));
         }
       };
 
