@@ -205,6 +205,8 @@ struct GemmTraits {
   static_assert(EPI == 4 || EPI == 8, "4 or 8 epilogue warps");
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(RING == 0 || (RING >= 2 && RING <= kWarpChunks), "a ring has 2 .. kWarpChunks slots");
+  static_assert(!(KIND == KIND_HEAD && BN == 256) || (CG == 2 && RING > 0),
+                "a head work item of two vocabulary tiles runs on a CTA pair with an output ring");
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB shared-memory limit");
 };
 
@@ -265,9 +267,30 @@ __device__ __forceinline__ void count_live(const GemmParams& p, int m_blk, int l
 template <int KIND, int BN>
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_blk, int& n_col0);
 
+// KIND_HEAD with BN = 256 (a CTA pair): work item t covers entries 2j and 2j + 1 of
+// the list of 128-column vocabulary tiles (col_tiles, or every tile in order), one
+// per CTA of the pair; an odd list leaves the last item with one tile, which runs
+// as a half-width item.  n_tiles counts 128-column tiles.  Returns the half flag.
+__device__ __forceinline__ bool head_pair_coords(const GemmParams& p, int t, int& m_blk, int& col0, int& col1) {
+  const int items = (p.n_tiles + 1) >> 1;
+  m_blk = t / items;
+  const int i0 = 2 * (t - m_blk * items);
+  col0 = (p.col_tiles != nullptr ? __ldg(p.col_tiles + i0) : i0) * 128;
+  const bool single = i0 + 1 >= p.n_tiles;
+  col1 = single ? col0 : (p.col_tiles != nullptr ? __ldg(p.col_tiles + i0 + 1) : i0 + 1) * 128;
+  return single;
+}
+
+template <int KIND, int BN>
+__host__ __device__ constexpr bool head_pairs() { return KIND == KIND_HEAD && BN == 256; }
+
 // Work item t -> its tile's M-block and first column; true for a half-width item.
 template <int KIND, int BN>
 __device__ __forceinline__ bool work_coords(const GemmParams& p, int t, int& m_blk, int& n_col0) {
+  if constexpr (head_pairs<KIND, BN>()) {
+    int col1;
+    return head_pair_coords(p, t, m_blk, n_col0, col1);
+  }
   if (t < p.tail_from) {
     tile_coords<KIND, BN>(p, t, m_blk, n_col0);
     return false;
@@ -498,7 +521,13 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       int m_blk, n_col0;
       const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
       const int a_row = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM;
-      const int b_row = n_col0 + static_cast<int>(rank) * ((half ? BN / 2 : BN) / CG);
+      int b_row = n_col0 + static_cast<int>(rank) * ((half ? BN / 2 : BN) / CG);
+      if constexpr (head_pairs<KIND, BN>()) {
+        // Each CTA of the pair loads its own vocabulary tile (BN / CG = 128 rows).
+        int mb, c0, c1;
+        head_pair_coords(p, t, mb, c0, c1);
+        if (!half) b_row = rank == 0 ? c0 : c1;
+      }
       // A half-width item loads half of B through the second B map (a box of BN/2/CG rows).
       const CUtensorMap* map_b = half ? &tm_b2 : &tm_b;
       const uint32_t stage_bytes = half ? Tr::kABytes + Tr::kBBytes / 2 : Tr::kStageBytes;
@@ -583,11 +612,14 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         const uint32_t idesc = half ? idesc_half : idesc_full;
         int live_blocks, live_steps;
         count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
-        // Counted per whole tile: a split tile's second half adds nothing.
-        if (!half || ((t - p.tail_from) & 1) == 0) {
-          skipped_steps += static_cast<unsigned long long>(k_steps_total - live_steps);
-          issued_steps += static_cast<unsigned long long>(live_steps);
-        }
+        // Counted per whole tile: a split tile's second half adds nothing.  A head
+        // item counts per 128-token x 128-column tile, as the single-CTA head does:
+        // its vocabulary tiles times the 128-token halves of its M-block in range.
+        unsigned long long weight = (!half || ((t - p.tail_from) & 1) == 0) ? 1ull : 0ull;
+        if constexpr (head_pairs<KIND, BN>())
+          weight = (half ? 1ull : 2ull) * (m_blk * Tr::kTileM + kBM < p.M ? 2ull : 1ull);
+        skipped_steps += weight * static_cast<unsigned long long>(k_steps_total - live_steps);
+        issued_steps += weight * static_cast<unsigned long long>(live_steps);
         // A tile without live K-blocks needs no MMA: the epilogue writes the
         // zero-accumulator result itself (the joint always has its z branch).
         if (KIND != KIND_JOINT && live_blocks == 0) continue;
@@ -663,10 +695,13 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31 (hardware rule: warp id % 4)
     constexpr int kMyChunks = Tr::kWarpChunks;
     constexpr int kBatches = (kMyChunks + Tr::kFlush - 1) / Tr::kFlush;
-    const int ch_begin = (ew / 4) * kMyChunks;  // EPI == 8: the two warps of a quarter split the columns
+    // EPI == 8: the two warps of a quarter split the columns of a tile (or of a
+    // half-width item) in two; this warp's first chunk of an item:
+    const int col_part = ew / 4;
+    auto first_chunk = [&](bool half) { return col_part * (half ? kMyChunks / 2 : kMyChunks); };
     constexpr bool kRing = RING > 0;
     uint8_t* stage_out = s_out + ew * Tr::kSlabChunks * Tr::kStageOutBytes;
-    float* bias_s = s_bias + ew * kMyChunks * 32;  // this warp's columns ch_begin*32 ..
+    float* bias_s = s_bias + ew * kMyChunks * 32;  // this warp's columns, from its first chunk on
     float* bias2_s = bias_s + EPI * kMyChunks * 32;  // KIND_JOINT: the second product's bias; KIND_UP: ln_c
     constexpr bool ln = LN && KIND == KIND_UP;
     constexpr bool kHasRes = KIND == KIND_DOWN || KIND == KIND_JOINT;
@@ -687,8 +722,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       uint4 raw = make_uint4(0u, 0u, 0u, 0u);
       if (bias_lane && bias != nullptr && t < total_tiles) {
         int mb, nc;
-        work_coords<KIND, BN>(p, t, mb, nc);
-        const int col = nc + ch_begin * 32 + lane * 8;
+        const bool hf = work_coords<KIND, BN>(p, t, mb, nc);
+        const int col = nc + first_chunk(hf) * 32 + lane * 8;
         if (col < p.N) raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(bias) + col));
       }
       return raw;
@@ -711,8 +746,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       lns_next[0] = lns_next[1] = lnc_next[0] = lnc_next[1] = z;
       if (bias_lane && t < total_tiles) {
         int mb, nc;
-        work_coords<KIND, BN>(p, t, mb, nc);
-        const int col = nc + ch_begin * 32 + lane * 8;
+        const bool hf = work_coords<KIND, BN>(p, t, mb, nc);
+        const int col = nc + first_chunk(hf) * 32 + lane * 8;
         if (col < p.N) {
           const float4* sp = reinterpret_cast<const float4*>(p.ln_s + col);
           const float4* cp = reinterpret_cast<const float4*>(p.ln_c + col);
@@ -728,6 +763,16 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     for (int t = unit; t < total_tiles; t += units) {
       int m_blk, n_col0;
       const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
+      // Output column of chunk ch: a pair of vocabulary tiles maps chunks 4.. to the second tile.
+      int n_col1 = n_col0;
+      if constexpr (head_pairs<KIND, BN>()) {
+        int mb, c0;
+        head_pair_coords(p, t, mb, c0, n_col1);
+      }
+      auto chunk_col = [&](int ch) {
+        if constexpr (head_pairs<KIND, BN>()) return ch < 4 ? n_col0 + ch * 32 : n_col1 + (ch - 4) * 32;
+        return n_col0 + ch * 32;
+      };
       int live_blocks = 1, live_steps = 0;
       if constexpr (KIND != KIND_UP) count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
       const int row0 = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
@@ -738,7 +783,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const float row_mean = (ln && row_ok) ? __ldg(p.ln_mean + row) : 0.f;
       const float row_rstd = (ln && row_ok) ? __ldg(p.ln_rstd + row) : 0.f;
       const bool has_h = live_blocks > 0;                             // KIND_JOINT: the h accumulator was written
-      const int ch_end = ch_begin + (half ? kMyChunks / 2 : kMyChunks);  // half: EPI == 4
+      const int ch_begin = first_chunk(half);
+      const int ch_end = ch_begin + (half ? kMyChunks / 2 : kMyChunks);
       // RING > 0: the residual of chunk ch (this thread's row, 32 values) into registers.
       auto load_res = [&](int ch, uint4 (&r)[4]) {
         if constexpr (kRing && kHasRes) {
@@ -826,7 +872,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this lane's row in a 32x32 chunk
       // v: the chunk's accumulator values (KIND_JOINT: of h W2^T, with v2 those of z Wo^T).
       auto process = [&](int ch, const uint32_t (&v)[32], const uint32_t (&v2)[32], const uint4 (&res_regs)[4]) {
-        const int col0 = n_col0 + ch * 32;
+        const int col0 = chunk_col(ch);
         const int slot = ch - ch_begin;
         uint8_t* buf = stage_out + (kRing ? ring_slot : slot) * Tr::kStageOutBytes;
         if constexpr (kRing) {

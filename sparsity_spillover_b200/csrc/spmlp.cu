@@ -58,6 +58,9 @@ constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 constexpr int kDownFineBN = 256, kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
 // Vocabulary head: 128 x 128 tiles on single CTAs.
 constexpr int kHeadStages = 4, kHeadEpiWarps = 8, kHeadRing = 2;
+// Dense and N-gated head: work items of two vocabulary tiles on a CTA pair (256 x 256).
+constexpr int kHeadPairStages = 5, kHeadPairEpiWarps = 8, kHeadPairRing = 2;
+constexpr int kHeadPairMinD = 256;  // d from which the pair kernel is faster (B200: d = 256 and 512 measured)
 // Joint consumer: 256 output columns per tile, so that h is read by only d/256
 // column tiles; the tile's two accumulators then fill TMEM's 512 columns and are
 // single-buffered (measured on cfg1: 96 us against 121 us for double-buffered
@@ -159,7 +162,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
   p.m_tiles = (p.M + Tr::kTileM - 1) / Tr::kTileM;
-  const int tiles = p.m_tiles * p.n_tiles;
+  // A head work item of BN = 256 holds two 128-column vocabulary tiles (n_tiles counts those).
+  const int n_items = head_pairs<KIND, BN>() ? (p.n_tiles + 1) / 2 : p.n_tiles;
+  const int tiles = p.m_tiles * n_items;
   if (tiles == 0) return 0;
   p.tail_from = p.work_items = tiles;
   p.status = dev->status;
@@ -637,9 +642,16 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
   constexpr int BN = 128;
-  CUtensorMap ta, tb;
+  // The K-gated head skips K16 groups dead for its 128 tokens (single CTA, one
+  // vocabulary tile per item).  The dense and N-gated heads with d >= 256 run two
+  // vocabulary tiles per item on a CTA pair (each CTA loads one tile of w_vocab,
+  // 128 rows), which halves the operand traffic per MMA; at small d the logit
+  // stores bound the head and the single-CTA kernel is faster.
+  const bool pairs = gate_axis != SPMLP_HEAD_GATE_K && d >= kHeadPairMinD;
+  CUtensorMap ta, tb, tb_half;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
   if ((rc = make_kmajor_map(&tb, w, V, d, BN, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb_half, w, V, d, BN / 2, bf16))) return rc;  // a lone tile split over the pair
   CUtensorMap tc;
   if ((rc = make_out_map(&tc, logits, T, V, bf16))) return rc;
   GemmParams p{};
@@ -655,6 +667,11 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   p.stats = reinterpret_cast<unsigned long long*>(stats);
   // Eight epilogue warps (two 32-column chunks each) and a two-slot output ring:
   // the logit stores, not the MMAs, bound the head at d = 128.
+  if (pairs) {
+    constexpr int SP = kHeadPairStages, EP = kHeadPairEpiWarps, RP = kHeadPairRing;
+    if (bf16) return launch_gemm<KIND_HEAD, 0, 2 * BN, SP, true, EP, 2, RP>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb_half);
+    return launch_gemm<KIND_HEAD, 0, 2 * BN, SP, false, EP, 2, RP>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb_half);
+  }
   constexpr int S = kHeadStages, E = kHeadEpiWarps, R = kHeadRing;
   if (bf16) return launch_gemm<KIND_HEAD, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev);
   return launch_gemm<KIND_HEAD, 0, BN, S, false, E, 1, R>(ta, tb, tc, p, stream, dev);

@@ -106,3 +106,29 @@ def test_sparse_head_module_masks_inactive_tiles():
     ref = ohead.logits(x.reshape(-1, d).cpu(), lin.weight.detach().cpu()[cols])
     assert omlp.max_rel_error(out.reshape(-1, V)[:, cols].cpu(), ref) <= TOL[torch.float16]
     assert bool(torch.isneginf(out.reshape(-1, V)[:, np.setdiff1d(np.arange(V), cols)]).all())
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("t,d", [(200, 128), (320, 512), (768, 512), (100, 1024)])
+@pytest.mark.parametrize("n_active", [1, 2, 3, 8])
+def test_n_gated_head_pairs_of_vocabulary_tiles(dtype, t, d, n_active):
+    """From d = 512 the dense and N-gated head run two listed vocabulary tiles per CTA
+    pair: odd lists (a lone last tile), unsorted and non-adjacent tiles, token counts
+    that leave a partial 256-token block; stats count per 128-token x 128-column tile,
+    as the single-CTA kernel (d = 128 here) does."""
+    from sparsity_spillover_b200 import ops
+
+    g = torch.Generator().manual_seed(7 * t + n_active)
+    x = torch.randn(t, d, generator=g).to(dtype)
+    w = _weights(d, dtype, seed=11)
+    tiles = torch.randperm(V // 128, generator=g)[:n_active].to(torch.int32)  # unsorted, scattered
+    sentinel = torch.full((t, V), 5.0, dtype=dtype, device="cuda")
+    stats = torch.zeros(2, dtype=torch.int64, device="cuda")
+    logits = ops.head_sparse(x.cuda(), w.cuda(), active_tiles=tiles.cuda(), logits=sentinel, stats=stats)
+    out = logits.cpu()
+    cols = np.concatenate([np.arange(k * 128, (k + 1) * 128) for k in tiles.tolist()])
+    ref = ohead.logits(x, w[cols])
+    assert omlp.max_rel_error(out[:, cols], ref) <= TOL[dtype]
+    assert bool((out[:, np.setdiff1d(np.arange(V), cols)] == 5.0).all())
+    m_tiles = -(-t // 128)
+    assert stats.cpu().tolist() == [n_active * m_tiles * (d // 16), 0]
