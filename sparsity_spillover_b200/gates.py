@@ -133,3 +133,23 @@ def resolve(gate: Any) -> GateSpec:
     if isinstance(gate, Mapping):
         return from_mapping(gate)
     return from_module(gate)
+
+
+HEAD_GATE_KEYS = frozenset({"operator", "kappa", "tile_tokens", "tile_features"})
+
+
+def validate_head_gate(spec: Any) -> float:
+    """The head-input gate of the vocabulary head: an explicit 16x16 corner gate.
+
+    Same acceptance rule and error as the reference's head
+    (runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.py:20-28): a mapping
+    with exactly the keys operator / kappa / tile_tokens / tile_features, operator
+    ``tile_corner_threshold``, 16 x 16 tiles and a finite, nonnegative, non-bool number kappa.
+    Returns kappa rounded to fp32 (the certificate compares the fp32 input with it)."""
+    if (not isinstance(spec, Mapping) or set(spec) != HEAD_GATE_KEYS
+            or spec["operator"] != "tile_corner_threshold"
+            or (spec["tile_tokens"], spec["tile_features"]) != (16, 16)
+            or isinstance(spec["kappa"], bool) or not isinstance(spec["kappa"], int | float)
+            or not math.isfinite(spec["kappa"]) or spec["kappa"] < 0):
+        raise ValueError("An explicit unchanged corner16x16 gate is required")
+    return float(torch.tensor(spec["kappa"], dtype=torch.float32))

@@ -31,7 +31,7 @@ import torch
 
 from types import MethodType
 
-from . import _lib, ops
+from . import _lib, gates, ops
 from .gates import GateSpec, resolve
 
 
@@ -98,7 +98,7 @@ class SparseHead(torch.nn.Module):
     """embed_out replacement: dense, K-gated (corner certificates) or N-gated (vocabulary tiles)."""
 
     def __init__(self, linear: torch.nn.Linear, *, kappa: float | None = None, active_tiles=None,
-                 dtype: torch.dtype = torch.float16, masked_value: float | None = None):
+                 dtype: torch.dtype = torch.float16, masked_value: float | None = None, skip: bool = True):
         super().__init__()
         if linear.bias is not None:
             raise ValueError("GPT-NeoX embed_out has no bias")
@@ -106,6 +106,7 @@ class SparseHead(torch.nn.Module):
             raise ValueError("choose the K gate (kappa) or the N gate (active_tiles)")
         self.weight = linear.weight  # original parameter, original state_dict name
         self.kappa = kappa
+        self.skip = skip  # K gate: skip dead K16 steps (False: certificates applied, every step issued)
         self.dtype = dtype
         self.masked_value = masked_value
         w = self.weight.detach()
@@ -123,6 +124,14 @@ class SparseHead(torch.nn.Module):
             self._active = tiles.to(self.weight.device)
             self._inactive = torch.nonzero(all_tiles).flatten().to(torch.int32).to(self.weight.device)
 
+    @classmethod
+    def from_spec(cls, linear: torch.nn.Linear, spec, *, skip: bool = True,
+                  dtype: torch.dtype = torch.float16) -> "SparseHead":
+        """The reference head's constructor form, Head(linear, spec, skip=...)
+        (runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.py:48-60): spec is
+        the explicit 16x16 corner gate of the head input (gates.validate_head_gate)."""
+        return cls(linear, kappa=gates.validate_head_gate(spec), dtype=dtype, skip=skip)
+
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         _inference_guard(hidden_states)
         shape = hidden_states.shape
@@ -130,12 +139,49 @@ class SparseHead(torch.nn.Module):
         support = None
         if self.kappa is not None:
             x, support = ops.head_prepare(x.float(), self.kappa, self.dtype)
+            if not self.skip:
+                support = None  # the zeroed tiles contribute exact zeros either way
         elif x.dtype != self.dtype:
             x = x.to(self.dtype)
         logits = ops.head_sparse(x, self._w, support=support, active_tiles=self._active)
         if self._inactive is not None and self.masked_value is not None and self._inactive.numel():
             ops.head_fill(logits, self._inactive, self.masked_value)
         return logits.view(*shape[:-1], logits.shape[-1])
+
+
+HEAD_MODES = ("dense", "custom_no_skip", "custom_sparse")
+
+
+def install_head(model: torch.nn.Module, mode: str, config: dict[str, Any] | None = None) -> dict[str, Any]:
+    """Replace ``model.embed_out`` as the reference's head installer does
+    (runs/068-2026-10-08-pythia14m-aligned-vocabulary-tiles/inference/head.py:93-112).
+
+    mode ``dense``: every logit from the sm_100a kernel, no gate; ``custom_no_skip``: the
+    head input's 16x16 corner certificates (``model.config.head_input_gate``) zero dead
+    tiles, every K16 step is issued; ``custom_sparse``: the same, dead K16 steps skipped.
+    ``config`` may carry the reference's consumer tile (``kernel_tile_tokens`` 16,
+    ``kernel_tile_vocabulary`` 128/256/512), validated as there and recorded; the kernel's
+    own tile is 128 tokens x 128 vocabulary columns (two per CTA pair for d >= 256, dense)."""
+    if mode not in HEAD_MODES:
+        raise ValueError(mode)
+    spec = getattr(model.config, "head_input_gate", None)
+    config = dict(config or {})
+    tile = (config.get("kernel_tile_tokens", 16), config.get("kernel_tile_vocabulary", 256))
+    if tile[0] != 16 or tile[1] not in (128, 256, 512):
+        raise ValueError("Unsupported consumer tile")
+    linear = model.embed_out
+    if isinstance(linear, SparseHead):
+        raise ValueError("embed_out is already replaced")
+    if mode == "dense":
+        head = SparseHead(linear)
+    else:
+        head = SparseHead.from_spec(linear, spec, skip=mode == "custom_sparse")
+    model.embed_out = head
+    return {"mode": mode, "gate": None if mode == "dense" else dict(spec), "gate_materialized": mode != "dense",
+            "parameters": "unchanged", "projection": "fp16 inputs and weights, fp32 accumulation, fp16 logits",
+            "static_weight_preparation": "one fp16 cast outside timing, no packed copy (w_vocab is K-major)",
+            "certificate": None if mode == "dense" else "fp32 corner > fp32 threshold before the cast",
+            "consumer_tile": [tile[0], tile[1], 16]}
 
 
 def install(model: torch.nn.Module, *, skip: bool = True) -> dict[str, Any]:

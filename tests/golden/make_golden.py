@@ -18,6 +18,7 @@ Every fixture is produced by executing the reference's modules, never the oracle
 * head.npz       runs/068-…/inference/head.py pack_weight; diagnostics.py counts() certificates.
 * measurement.npz runs/025-…/measurement.py paired_schedule (several counts, passes, mode lists and
                  seeds) and timing_summary on fixed synthetic samples.
+* head_gate.npz  runs/068-…/inference/head.py validate_gate on accepted and rejected head-input specs.
 """
 from __future__ import annotations
 
@@ -183,6 +184,31 @@ def head(ref: Path) -> dict:
     return out
 
 
+def head_gate_cases() -> list:
+    """Head-input gate specs: accepted ones and every way the reference rejects one."""
+    ok = {"operator": "tile_corner_threshold", "kappa": 0.1, "tile_tokens": 16, "tile_features": 16}
+    return [ok, dict(ok, kappa=0), dict(ok, kappa=3), dict(ok, kappa=1e-30), dict(ok, kappa=0.3333333333),
+            dict(ok, kappa=-0.1), dict(ok, kappa=float("inf")), dict(ok, kappa=float("nan")), dict(ok, kappa=True),
+            dict(ok, kappa="0.1"), dict(ok, operator="one_sided_threshold"), dict(ok, tile_tokens=8),
+            dict(ok, tile_features=32), {k: v for k, v in ok.items() if k != "tile_features"},
+            dict(ok, extra=1), None, [("kappa", 0.1)]]
+
+
+def head_gate(ref: Path) -> dict:
+    sys.path.insert(0, str(ref / R068))
+    try:
+        head_mod = load("golden_head_gate", ref / R068 / "head.py")
+    finally:
+        sys.path.pop(0)
+    values = []
+    for spec in head_gate_cases():
+        try:
+            values.append(head_mod.validate_gate(spec))
+        except ValueError:
+            values.append(float("nan"))  # rejected
+    return {"kappa_or_nan": np.array(values, dtype=np.float64)}
+
+
 # (count, passes, modes, seed) cases of the paired schedule
 SCHEDULE_CASES = [(1, 1, ("native",), 0), (3, 2, ("native", "fused", "sparse"), 7),
                   (4, 3, ("dense_pytorch", "ours_rho100", "ours_rho10"), 2026), (5, 2, ("a", "b"), 123456789)]
@@ -219,7 +245,7 @@ def main():
     torch.set_num_threads(1)
     for name, fn in (("gates", lambda: gates(ref)), ("mlp_cfg0", mlp_cfg0), ("counts", lambda: counts(ref)),
                      ("joint", lambda: joint(ref)), ("head", lambda: head(ref)),
-                     ("measurement", lambda: measurement(ref))):
+                     ("measurement", lambda: measurement(ref)), ("head_gate", lambda: head_gate(ref))):
         if args.only and name not in args.only:
             continue
         arrays = fn()

@@ -55,3 +55,35 @@ def test_install_matches_unfused_model_for_prefill_and_decode(dtype):
     assert omlp.max_rel_error(out.logits.float().cpu(), ref_logits.cpu()) <= tol
     assert omlp.max_rel_error(step.cpu(), ref_step.cpu()) <= tol
     assert step2.shape == (2, 1, 1024) and bool(torch.isfinite(step2).all())
+
+
+@pytest.mark.parametrize("mode", ["custom_sparse", "custom_no_skip", "dense"])
+def test_install_head_matches_the_oracle_on_the_final_hidden_states(mode):
+    """install_head(model, mode, config) as the reference's head installer: the fp32 model's
+    final hidden states, their 16x16 corner certificates (custom modes) and an fp16 projection
+    give the oracle's logits."""
+    import transformers
+
+    from oracle import head as ohead
+    from sparsity_spillover_b200 import install_head
+
+    cfg = transformers.GPTNeoXConfig(hidden_size=128, intermediate_size=512, num_hidden_layers=2,
+                                     num_attention_heads=4, vocab_size=2048, attn_implementation="eager")
+    torch.manual_seed(68)
+    model = transformers.GPTNeoXForCausalLM(cfg).cuda().eval()
+    kappa = 0.25
+    model.config.head_input_gate = {"operator": "tile_corner_threshold", "kappa": kappa, "tile_tokens": 16,
+                                    "tile_features": 16}
+    ids = torch.randint(0, 2048, (1, 128), device="cuda")
+    with torch.inference_mode():
+        hidden = model.gpt_neox(ids).last_hidden_state.float().cpu()[0]
+        meta = install_head(model, mode, {"kernel_tile_tokens": 16, "kernel_tile_vocabulary": 256})
+        logits = model(ids).logits.float().cpu()[0]
+    w = model.embed_out.weight.detach().cpu().half()
+    if mode == "dense":
+        ref = ohead.logits(hidden.half(), w)
+    else:
+        x_ref, _ = ohead.prepare(hidden, kappa, torch.float16)
+        ref = ohead.logits(x_ref, w)
+        assert meta["gate"]["kappa"] == kappa
+    assert omlp.max_rel_error(logits, ref.float()) <= 2e-3

@@ -275,3 +275,66 @@ def test_bitmap_pack_roundtrip_and_skip_counts():
     # First 128-token tile: both 64-feature K-blocks live (4 K16 steps each); second tile: none.
     issued, skipped = obit.skip_counts(m, 128, n_tiles=2)
     assert (issued, skipped) == (2 * 4 * 2, (2 * 8 - 2 * 4) * 2)
+
+
+def _golden_module():
+    import importlib.util
+
+    path = Path(__file__).parent / "golden" / "make_golden.py"
+    spec = importlib.util.spec_from_file_location("make_golden_cases", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_head_gate_validation_matches_the_reference():
+    """gates.validate_head_gate accepts and rejects exactly what the reference head's
+    validate_gate does (golden outcomes from runs/068-…/inference/head.py:20-28)."""
+    from sparsity_spillover_b200 import gates
+
+    cases = _golden_module().head_gate_cases()
+    expect = np.load(Path(__file__).parent / "golden" / "head_gate.npz")["kappa_or_nan"]
+    assert len(cases) == len(expect)
+    for spec, want in zip(cases, expect):
+        if np.isnan(want):
+            with pytest.raises(ValueError, match="corner16x16"):
+                gates.validate_head_gate(spec)
+        else:
+            assert gates.validate_head_gate(spec) == want
+
+
+def test_install_head_modes_and_checks_on_cpu():
+    """The reference head installer's modes, consumer-tile rule and metadata (construction
+    only: no kernel runs without a GPU)."""
+    import transformers
+
+    from sparsity_spillover_b200 import SparseHead, install_head
+
+    def model():
+        cfg = transformers.GPTNeoXConfig(hidden_size=128, intermediate_size=512, num_hidden_layers=1,
+                                         num_attention_heads=4, vocab_size=1024)
+        m = transformers.GPTNeoXForCausalLM(cfg).eval()
+        m.config.head_input_gate = {"operator": "tile_corner_threshold", "kappa": 0.25, "tile_tokens": 16,
+                                    "tile_features": 16}
+        return m
+
+    with pytest.raises(ValueError):
+        install_head(model(), "bogus")
+    with pytest.raises(ValueError, match="consumer tile"):
+        install_head(model(), "custom_sparse", {"kernel_tile_tokens": 16, "kernel_tile_vocabulary": 64})
+    m = model()
+    m.config.head_input_gate = {"operator": "tile_corner_threshold", "kappa": 0.25}
+    with pytest.raises(ValueError, match="corner16x16"):
+        install_head(m, "custom_sparse")
+    for mode, skip in (("custom_sparse", True), ("custom_no_skip", False)):
+        m = model()
+        w = m.embed_out.weight
+        meta = install_head(m, mode, {"kernel_tile_tokens": 16, "kernel_tile_vocabulary": 128})
+        assert isinstance(m.embed_out, SparseHead) and m.embed_out.weight is w
+        assert m.embed_out.kappa == float(torch.tensor(0.25, dtype=torch.float32)) and m.embed_out.skip is skip
+        assert meta["mode"] == mode and meta["gate"]["kappa"] == 0.25 and meta["consumer_tile"] == [16, 128, 16]
+        with pytest.raises(ValueError, match="already"):
+            install_head(m, mode)
+    m = model()
+    meta = install_head(m, "dense")
+    assert m.embed_out.kappa is None and meta["gate"] is None
