@@ -481,18 +481,27 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
                                   y=bufs[i % 2])
         return cur
 
-    fused = sdist.FusedDffSplit(split, t_rank * world)
-
-    def run_fused():
-        return fused.forward(x_all)
-
+    # The fused split in both forms: partials stored into peers' receive buffers, and the
+    # reduction + broadcast through NVSwitch multicast (when the system offers it).
+    fused_peer = sdist.FusedDffSplit(split, t_rank * world, multicast=False)
+    runs = [("dff_split", run_split), ("dff_split_fused_peer", lambda: fused_peer.forward(x_all))]
+    fused_mc = None
+    if sdist.multicast_available(device):
+        fused_mc = sdist.FusedDffSplit(split, t_rank * world, multicast=True)
+        runs.append(("dff_split_fused_multicast", lambda: fused_mc.forward(x_all)))
+    runs.append(("token_sharded", run_tokens))
     out = {}
-    for name, fn in (("dff_split", run_split), ("dff_split_fused", run_fused), ("token_sharded", run_tokens)):
+    for name, fn in runs:
         fn()
         dist.barrier(device_ids=[device.index])
         t = max_over_ranks(time_device(fn, steps, device), world, device)
         out[f"{name}_tokens_per_s"] = world * t_rank / t
         out[f"{name}_ms_per_step"] = t * 1e3
+    # the product's default choice at this world size (FusedDffSplit(multicast=None))
+    chosen = "multicast" if fused_mc is not None and world >= sdist.FusedDffSplit.MULTICAST_MIN_WORLD else "peer"
+    out["dff_split_fused_tokens_per_s"] = out[f"dff_split_fused_{chosen}_tokens_per_s"]
+    out["dff_split_fused_ms_per_step"] = out[f"dff_split_fused_{chosen}_ms_per_step"]
+    out["dff_split_fused_form"] = chosen
     out.update(layers=layers, tokens_per_rank=t_rank, world=world,
                collective_bytes_per_layer=2 * (world - 1) * t_rank * cfg.d * 2)
     return out

@@ -167,6 +167,19 @@ int spmlp_down_scatter(const void* h, const uint32_t* tile_bits, const void* w_o
                        int64_t T, int F, int d, int dtype, int mode, uint64_t* stats, void* stream);
 int spmlp_reduce_broadcast(const void* recv, int world, int64_t rows, int d, const void* b_out,
                            const void* residual, void* const* targets, int n_targets, int dtype, void* stream);
+/* The same finish of the layer through NVLink SHARP, replacing the reduce-scatter +
+ * all-gather pair (ncclReduceScatter / ncclAllGather) of a d_ff split where the
+ * GPUs' memory is bound to an NVSwitch multicast object.  Every rank has written
+ * its rounded partial of all T tokens ([T, d], no bias, e.g. spmlp_down_sparse)
+ * into its own copy of a multicast-bound buffer, and the caller has ordered those
+ * writes before this call on every rank (spmlp_peer_barrier).  For this rank's
+ * block (rows tokens): mc_part is the block's address in the partial buffer's
+ * multicast mapping, mc_x in the next input's; residual is the block in this
+ * rank's local copy of the layer input (nullable).  y = round(round(s + b_out) +
+ * residual) with s = round(sum over ranks), reduced in fp32 inside the switch
+ * (multimem.ld_reduce .acc::f32), then written to every rank's copy (multimem.st). */
+int spmlp_reduce_broadcast_multicast(const void* mc_part, void* mc_x, const void* residual, int64_t rows, int d,
+                                     const void* b_out, int dtype, void* stream);
 /* Barrier between the ranks of the fused d_ff split over NVLink peer memory,
  * ordered on `stream`: this rank stores `epoch` into peer_slots[j] (its slot in
  * rank j's int64 flag array, [world]) after a system-scope fence, then waits until

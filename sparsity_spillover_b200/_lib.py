@@ -33,6 +33,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_down_sparse": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_down_scatter": (I32, [VP, VP, VP, _c.POINTER(VP), I32, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_reduce_broadcast": (I32, [VP, I32, I64, I32, VP, VP, _c.POINTER(VP), I32, I32, VP]),
+    "spmlp_reduce_broadcast_multicast": (I32, [VP, VP, VP, I64, I32, VP, I32, VP]),
     "spmlp_peer_barrier": (I32, [_c.POINTER(VP), VP, I32, I64, VP]),
     "spmlp_joint": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_gate": (I32, [VP, VP, VP, I64, I32, I32, I32, F32, VP]),

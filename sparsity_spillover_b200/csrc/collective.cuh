@@ -57,6 +57,69 @@ __global__ void __launch_bounds__(256) reduce_broadcast_kernel(const uint16_t* _
   __threadfence_system();  // peer stores are performed before the kernel completes
 }
 
+// The same finish of the layer through NVLink SHARP (NVSwitch multicast objects):
+// every rank has written its rounded partial of ALL tokens into its own copy of a
+// multicast-bound buffer; for this rank's block, multimem.ld_reduce returns the sum
+// of every rank's copy, reduced inside the switch in fp32 (.acc::f32) and rounded
+// once to the dtype; then y = round(round(sum + b_out) + residual) goes to every
+// rank's copy of the next layer's input with one multimem.st.  Per rank, the partial
+// tokens cross NVLink once into the switch and the result once out of it, instead
+// of one peer store per rank for each.  The switch's reduction order is fixed per
+// address, so every run gives the same y; it is not the rank order of
+// reduce_broadcast_kernel, and the sum is rounded once more before b_out is added.
+// mc_part / mc_x: this rank's block inside the multicast mappings; residual: this
+// rank's block of its local copy of the layer input (read before mc_x overwrites it).
+template <bool BF16>
+__device__ __forceinline__ uint4 multimem_ld_reduce_add_v4(const uint16_t* mc) {
+  uint4 v;
+  if constexpr (BF16)
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(mc) : "memory");
+  else
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(mc) : "memory");
+  return v;
+}
+
+template <bool BF16>
+__device__ __forceinline__ void multimem_st_v4(uint16_t* mc, const uint4& v) {
+  if constexpr (BF16)
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};"
+                 :: "l"(mc), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+  else
+    asm volatile("multimem.st.relaxed.sys.global.v4.f16x2 [%0], {%1, %2, %3, %4};"
+                 :: "l"(mc), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) multicast_reduce_broadcast_kernel(const uint16_t* mc_part, uint16_t* mc_x,
+                                                                         int64_t elems, int d,
+                                                                         const uint16_t* __restrict__ bias,
+                                                                         const uint16_t* residual) {
+  using D = DType<BF16>;
+  const int64_t vecs = elems / 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 sv = multimem_ld_reduce_add_v4<BF16>(mc_part + 8 * i);
+    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+    const int col = static_cast<int>((i * 8) % d);
+    uint4 b = make_uint4(0u, 0u, 0u, 0u);
+    if (bias != nullptr) b = __ldg(reinterpret_cast<const uint4*>(bias + col));
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(sw[j]) + D::lo(bw[j]), D::hi(sw[j]) + D::hi(bw[j]));
+    if (residual != nullptr) {
+      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(rw[j]), D::hi(out[j]) + D::hi(rw[j]));
+    }
+    multimem_st_v4<BF16>(mc_x + 8 * i, make_uint4(out[0], out[1], out[2], out[3]));
+  }
+  __threadfence_system();  // the multicast stores are performed before the kernel completes
+}
+
 struct PeerFlags {
   long long* dst[kMaxRanks];  // this rank's slot in each rank's flag array (peer memory)
 };

@@ -510,6 +510,33 @@ int row_stats_impl(const void* x, float* mean, float* rstd, int64_t T, int d, in
   return 0;
 }
 
+int multicast_reduce_broadcast_impl(const void* mc_part, void* mc_x, const void* residual, int64_t rows, int d,
+                                    const void* b_out, int dtype, cudaStream_t stream) {
+  int rc;
+  if (!mc_part || !mc_x) return fail(SPMLP_EINVAL, "mc_part and mc_x must be non-null multicast addresses");
+  if ((rc = check_dtype(dtype))) return rc;
+  if (rows < 1 || rows >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "rows must be in [1, 2^31)");
+  if (d < kBitsCols || d % kBitsCols) return fail(SPMLP_ESHAPE, "d=%d must be a positive multiple of 64", d);
+  if (!aligned16(mc_part) || !aligned16(mc_x) || (b_out && !aligned16(b_out)) || (residual && !aligned16(residual)))
+    return fail(SPMLP_EALIGN, "mc_part, mc_x, b_out and residual must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int64_t elems = rows * d;
+  const int64_t vecs = elems / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, int64_t(dev->sm_count) * 8));
+  const uint16_t* pv = static_cast<const uint16_t*>(mc_part);
+  uint16_t* xv = static_cast<uint16_t*>(mc_x);
+  const uint16_t* bv = static_cast<const uint16_t*>(b_out);
+  const uint16_t* resv = static_cast<const uint16_t*>(residual);
+  if (dtype == SPMLP_BF16)
+    multicast_reduce_broadcast_kernel<true><<<blocks, 256, 0, stream>>>(pv, xv, elems, d, bv, resv);
+  else
+    multicast_reduce_broadcast_kernel<false><<<blocks, 256, 0, stream>>>(pv, xv, elems, d, bv, resv);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "multicast_reduce_broadcast_kernel launch");
+  return 0;
+}
+
 int reduce_broadcast_impl(const void* recv, int world, int64_t rows, int d, const void* b_out, const void* residual,
                           void* const* targets, int n_targets, int dtype, cudaStream_t stream) {
   int rc;
@@ -931,6 +958,12 @@ int spmlp_reduce_broadcast(const void* recv, int world, int64_t rows, int d, con
                            void* const* targets, int n_targets, int dtype, void* stream) {
   return reduce_broadcast_impl(recv, world, rows, d, b_out, residual, targets, n_targets, dtype,
                                static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_reduce_broadcast_multicast(const void* mc_part, void* mc_x, const void* residual, int64_t rows, int d,
+                                     const void* b_out, int dtype, void* stream) {
+  return multicast_reduce_broadcast_impl(mc_part, mc_x, residual, rows, d, b_out, dtype,
+                                         static_cast<cudaStream_t>(stream));
 }
 
 int spmlp_joint(const void* h, const uint32_t* tile_bits, const void* z, const void* w2, const void* b2,

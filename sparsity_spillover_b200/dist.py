@@ -151,6 +151,24 @@ def dff_split_forward(layers: list[DffSplitMLP], x: torch.Tensor) -> torch.Tenso
     return shard
 
 
+def multicast_available(device: torch.device) -> bool:
+    """Whether torch symmetric memory on ``device`` can bind NVSwitch multicast objects."""
+    from torch.distributed._symmetric_memory import DeviceType, _SymmetricMemory
+
+    return device.type == "cuda" and bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index))
+
+
+def _multicast_ok(handle) -> bool:
+    """Whether a symmetric-memory rendezvous handle has an NVSwitch multicast mapping:
+    the device supports multicast and the rendezvous produced a multicast address."""
+    from torch.distributed._symmetric_memory import DeviceType, _SymmetricMemory
+
+    device = handle.device
+    if device.type != "cuda" or not _SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index):
+        return False
+    return int(handle.multicast_ptr or 0) != 0
+
+
 class FusedDffSplit:
     """A stack of d_ff-split layers with the reduce-scatter and all-gather fused into
     the kernels (``spmlp_down_scatter`` / ``spmlp_reduce_broadcast``) over NVLink.
@@ -165,9 +183,22 @@ class FusedDffSplit:
     waits); NCCL is used only once, to order the flags' initialisation.  X, the receive
     buffers and the flags are torch symmetric-memory tensors, so peers' addresses come
     from its rendezvous; tokens per rank must be a multiple of 256; one rank per GPU.
+
+    ``multicast`` (NVLink SHARP): each rank's down projection writes its partial of
+    all tokens into its own copy of a multicast-bound buffer; after the barrier,
+    ``spmlp_reduce_broadcast_multicast`` reduces this rank's block inside the switch
+    (multimem.ld_reduce) and writes the result to every rank's X (multimem.st).  Per
+    rank and layer that moves the partial tokens once into the switch and the block
+    once out of it, against (w-1)/w of the partials out and in again for the peer
+    stores, so it pays from four ranks on.  None (default): multicast when the
+    symmetric memory supports it and world >= 4.  Set False where a rank may die while
+    the others run (a multicast-bound peer that disappears can fault the others).
     """
 
-    def __init__(self, layers: list[DffSplitMLP], tokens: int, *, skip: bool | str = True):
+    MULTICAST_MIN_WORLD = 4
+
+    def __init__(self, layers: list[DffSplitMLP], tokens: int, *, skip: bool | str = True,
+                 multicast: bool | None = None):
         import torch.distributed._symmetric_memory as symm_mem
 
         from . import ops
@@ -187,20 +218,42 @@ class FusedDffSplit:
         self.skip = skip
         group = self.group or dist.group.WORLD
         self.x = symm_mem.empty((tokens, self.d), dtype=self.dtype, device=self.device)
-        self.recv = symm_mem.empty((self.world, self.rows, self.d), dtype=self.dtype, device=self.device)
         hx = symm_mem.rendezvous(self.x, group)
-        hr = symm_mem.rendezvous(self.recv, group)
         esize = self.x.element_size()
         block = self.rows * self.d * esize
-        # My slot in each rank's receive buffer, and my token block in each rank's X.
-        self.slots = [int(hr.buffer_ptrs[j]) + self.rank * block for j in range(self.world)]
-        self.targets = [int(hx.buffer_ptrs[j]) + self.rank * block for j in range(self.world)]
+        # A tensor may sit at an offset inside its symmetric buffer; peers' copies and the
+        # multicast mapping put it at the same offset.
+        off_x = self.x.data_ptr() - int(hx.buffer_ptrs[self.rank])
+        supported = _multicast_ok(hx)
+        if multicast is None:
+            multicast = supported and self.world >= self.MULTICAST_MIN_WORLD
+        if multicast and not supported:
+            raise RuntimeError("symmetric memory on this system has no NVSwitch multicast support")
+        self.multicast = bool(multicast)
+        if self.multicast:
+            # Partials of all tokens, one copy per rank, bound to a multicast object.
+            self.part = symm_mem.empty((tokens, self.d), dtype=self.dtype, device=self.device)
+            hr = symm_mem.rendezvous(self.part, group)
+            if not _multicast_ok(hr):
+                raise RuntimeError("the partial buffer got no multicast mapping")
+            off_p = self.part.data_ptr() - int(hr.buffer_ptrs[self.rank])
+            self.mc_part = int(hr.multicast_ptr) + off_p + self.rank * block  # my block, multicast addresses
+            self.mc_x = int(hx.multicast_ptr) + off_x + self.rank * block
+            self.slots = self.targets = []
+        else:
+            self.recv = symm_mem.empty((self.world, self.rows, self.d), dtype=self.dtype, device=self.device)
+            hr = symm_mem.rendezvous(self.recv, group)
+            off_r = self.recv.data_ptr() - int(hr.buffer_ptrs[self.rank])
+            # My slot in each rank's receive buffer, and my token block in each rank's X.
+            self.slots = [int(hr.buffer_ptrs[j]) + off_r + self.rank * block for j in range(self.world)]
+            self.targets = [int(hx.buffer_ptrs[j]) + off_x + self.rank * block for j in range(self.world)]
         self.h = torch.empty((tokens, self.f), dtype=self.dtype, device=self.device)
         self.bits = torch.empty((ops.tile_bits_size(tokens, self.f),), dtype=torch.int32, device=self.device)
         self.flags = symm_mem.empty((self.world,), dtype=torch.int64, device=self.device)
         self.flags.zero_()
         hf = symm_mem.rendezvous(self.flags, group)
-        self.flag_slots = [int(hf.buffer_ptrs[j]) + self.rank * 8 for j in range(self.world)]
+        off_f = self.flags.data_ptr() - int(hf.buffer_ptrs[self.rank])
+        self.flag_slots = [int(hf.buffer_ptrs[j]) + off_f + self.rank * 8 for j in range(self.world)]
         self._handles = (hx, hr, hf)
         self.epoch = 0
         torch.cuda.synchronize(self.device)
@@ -227,8 +280,14 @@ class FusedDffSplit:
         mine = self.x[self.rank * self.rows:(self.rank + 1) * self.rows]
         for layer in self.layers:
             ops.up_gate(self.x, layer.w_in, layer.b_in, layer.gate, h=self.h, bits=self.bits)
-            ops.down_scatter(self.h, self.bits, layer.w_out, self.slots, skip=self.skip)
-            self._barrier()
-            ops.reduce_broadcast(self.recv, layer.b_out, mine, self.targets)
+            if self.multicast:
+                ops.down_sparse(self.h, self.bits, layer.w_out, None, None, skip=self.skip, y=self.part)
+                self._barrier()
+                ops.reduce_broadcast_multicast(self.mc_part, self.mc_x, self.rows, self.d, layer.b_out, mine,
+                                               self.dtype, self.device)
+            else:
+                ops.down_scatter(self.h, self.bits, layer.w_out, self.slots, skip=self.skip)
+                self._barrier()
+                ops.reduce_broadcast(self.recv, layer.b_out, mine, self.targets)
             self._barrier()
         return mine

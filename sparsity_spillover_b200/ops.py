@@ -316,6 +316,25 @@ def reduce_broadcast(recv: torch.Tensor, b_out: torch.Tensor | None, residual: t
     del keep
 
 
+def reduce_broadcast_multicast(mc_part: int, mc_x: int, rows: int, d: int, b_out: torch.Tensor | None,
+                               residual: torch.Tensor | None, dtype: torch.dtype, device: torch.device) -> None:
+    """The d_ff split's reduction + broadcast through NVSwitch multicast (include/spmlp.h):
+    ``mc_part`` / ``mc_x`` are this rank's block addresses in the multicast mappings of the
+    partial buffer and of the next layer's input; ``residual`` is the block in the local copy."""
+    code = _DTYPES[dtype] if dtype in _DTYPES else None
+    if code is None:
+        raise TypeError(f"unsupported dtype {dtype}")
+    if b_out is not None:
+        _check("b_out", b_out, dtype, device, (d,))
+    if residual is not None:
+        _check("residual", residual, dtype, device, (rows, d))
+    if not mc_part or not mc_x:
+        raise ValueError("multicast addresses must be nonzero")
+    with torch.cuda.device(device):
+        _lib.call("spmlp_reduce_broadcast_multicast", int(mc_part), int(mc_x), _ptr(residual), int(rows), int(d),
+                  _ptr(b_out), code, _stream(device))
+
+
 def peer_barrier(peer_slots: list[int], local_flags: torch.Tensor, epoch: int) -> None:
     """Device-side barrier of the fused d_ff split over NVLink (see include/spmlp.h)."""
     device = local_flags.device

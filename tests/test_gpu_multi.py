@@ -56,7 +56,7 @@ def _worker(rank, world, port, queue):
         whole = ops.mlp_forward(x, full[0].w_in, full[0].b_in, full[0].w_out, full[0].b_out, gate)
         same = bool(torch.equal(tok, whole[lo:hi]))
         # the fused d_ff split: P2P scatter from the down projection, reduction + broadcast kernel
-        fused = sdist.FusedDffSplit(layers, t)
+        fused = sdist.FusedDffSplit(layers, t, multicast=False)  # peer stores (the failure test below)
         y_fused = fused.forward(x)
         err_fused = omlp.max_rel_error(y_fused.float().cpu(), ref[lo:hi].float().cpu())
         full_x = fused.x.clone()
@@ -104,3 +104,79 @@ def test_dff_split_over_nccl_and_token_shards():
         assert same_again
         assert rows_ok <= 2e-2, (rank, rows_ok)
         assert timeout_status == 6 and usable  # SPMLP_STATUS_TIMEOUT_PEER
+
+
+def _multicast_worker(rank, world, port, queue):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from oracle import mlp as omlp
+        from sparsity_spillover_b200 import dist as sdist
+        from sparsity_spillover_b200 import ops, workloads
+
+        probe = symm_mem.empty((256,), dtype=torch.float16, device=dev)
+        supported = sdist._multicast_ok(symm_mem.rendezvous(probe, dist.group.WORLD))
+        result = {"rank": rank, "supported": supported}
+        if supported:
+            cfg = workloads.CONFIGS["cfg3"]
+            t = 4096
+            full = workloads.make_weights(cfg, dev)[:2]
+            gate = {"operator": "one_sided_threshold", "kappa": 0.5}
+            x = workloads.make_input(cfg, dev, tokens=t)
+            layers = [sdist.DffSplitMLP.from_full(L.w_in, L.b_in, L.w_out, L.b_out, gate, world, rank) for L in full]
+            ref = x
+            for L in full:
+                ref = ops.mlp_forward(ref, L.w_in, L.b_in, L.w_out, L.b_out, gate, residual=ref)
+            lo, hi = rank * t // world, (rank + 1) * t // world
+            mc = sdist.FusedDffSplit(layers, t, multicast=True)
+            y = mc.forward(x).clone()
+            full_x = mc.x.clone()
+            y2 = mc.forward(x).clone()
+            peer = sdist.FusedDffSplit(layers, t, multicast=False)
+            y_peer = peer.forward(x).clone()
+            torch.cuda.synchronize(dev)
+            result.update(multicast=mc.multicast, err=omlp.max_rel_error(y.float().cpu(), ref[lo:hi].float().cpu()),
+                          rows_ok=omlp.max_rel_error(full_x.float().cpu(), ref.float().cpu()),
+                          same_again=bool(torch.equal(y, y2)),
+                          vs_peer=omlp.max_rel_error(y.float().cpu(), y_peer.float().cpu()),
+                          status=ops.device_status(rank))
+        queue.put(result)
+    finally:
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_dff_split_through_nvswitch_multicast():
+    """The d_ff split's reduction + broadcast through NVLink SHARP (multimem.ld_reduce,
+    multimem.st) matches one GPU and the peer-store form within tolerance, gives the
+    same result on a second call, and leaves every block on every rank.  No rank fails
+    here: failure detection runs on the peer-store form only."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_multicast_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    if not all(r["supported"] for r in results):
+        pytest.skip("no NVSwitch multicast support for symmetric memory on this system")
+    for r in results:
+        assert r["multicast"] and r["status"] == 0
+        assert r["err"] <= 2e-2, r  # fp16 partials reduced in fp32 in the switch, rounded, then bias / residual
+        assert r["rows_ok"] <= 2e-2, r
+        assert r["same_again"], r
+        assert r["vs_peer"] <= 2e-2, r
