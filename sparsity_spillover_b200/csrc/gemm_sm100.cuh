@@ -53,6 +53,7 @@ constexpr int kBK = 64;        // K elements per pipeline stage (one 128-byte sw
 constexpr int kBitsRows = 16;  // bitmap tile height (tokens)
 constexpr int kBitsCols = 64;  // bitmap tile width (features)
 constexpr int kMaxRanks = 8;   // ranks a scattering down projection can address
+constexpr int kPrefetchAhead = 8;  // K-blocks of h brought into L2 ahead of their TMA loads
 
 struct GemmParams {
   int M, N, K;            // tokens, output columns, reduction length
@@ -247,6 +248,47 @@ __device__ __forceinline__ bool for_each_live_kblock(const GemmParams& p, int m_
         pending &= pending - 1;
         if (!f(c * 8 + i, (mask >> (4 * i)) & 0xFu)) return false;
       }
+    }
+  }
+  return true;
+}
+
+// for_each_live_kblock for the TMA producer, which also calls pf(kb) for the live
+// K-block AHEAD positions further on in the same 32-granule chunk of the bitmap (the
+// first AHEAD blocks of a chunk as it starts), so that their operand tiles can be
+// brought into L2 before the shared-memory ring has room for them.
+template <int KIND, int GROUPS, int AHEAD, class F, class P>
+__device__ __forceinline__ bool for_each_live_kblock_ahead(const GemmParams& p, int m_blk, int lane, F&& f, P&& pf) {
+  const int kblocks = p.K / kBK;
+  if (!p.skip || p.bits_in == nullptr) {
+    for (int kb = 0; kb < AHEAD && kb < kblocks; ++kb) pf(kb);
+    for (int kb = 0; kb < kblocks; ++kb) {
+      if (kb + AHEAD < kblocks) pf(kb + AHEAD);
+      if (!f(kb, 0xFu)) return false;
+    }
+    return true;
+  }
+  const int row_groups = (p.M + kBitsRows - 1) / kBitsRows;
+  const int granules = k_granules<KIND>(p.K);
+  const int chunks = (granules + 31) / 32;
+  constexpr int kPerChunk = KGran<KIND>::value == kBK ? 32 : 8;  // K-blocks per chunk of 32 granules
+  for (int c = 0; c < chunks; ++c) {
+    const uint32_t mask = live_chunk<GROUPS>(p.bits_in, p.bits_words, row_groups, m_blk, c, granules, lane);
+    uint32_t pending = KGran<KIND>::value == kBK ? mask : kblocks_of_k16(mask);
+    uint32_t ahead = pending;
+    for (int i = 0; i < AHEAD && ahead; ++i) {
+      pf(c * kPerChunk + __ffs(ahead) - 1);
+      ahead &= ahead - 1;
+    }
+    while (pending) {
+      const int i = __ffs(pending) - 1;
+      pending &= pending - 1;
+      if (ahead) {
+        pf(c * kPerChunk + __ffs(ahead) - 1);
+        ahead &= ahead - 1;
+      }
+      const uint32_t k16 = KGran<KIND>::value == kBK ? 0xFu : (mask >> (4 * i)) & 0xFu;
+      if (!f(c * kPerChunk + i, k16)) return false;
     }
   }
   return true;
@@ -565,8 +607,20 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         for (int kb = 0; kb < p.K2 / kBK && ok; ++kb) ok = issue(&tm_a2, &tm_b2, kb);
         if (!ok) break;
       }
-      ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane,
-                                               [&](int kb, uint32_t) { return issue(&tm_a, map_b, kb); });
+      if constexpr ((KIND == KIND_DOWN || KIND == KIND_JOINT) && CG == 1) {
+        // A is h, mostly in HBM (written by the up projection, larger than L2): bring
+        // its tiles into L2 kPrefetchAhead live K-blocks ahead of the loads.  This pays
+        // for the single-CTA skipping kernels (4-6 % on tile-structured h); the pair
+        // kernels are bound by the L2-to-SM operand stream instead, and lose 2-7 %.
+        ok = for_each_live_kblock_ahead<KIND, kGroups, kPrefetchAhead>(
+            p, m_blk, lane, [&](int kb, uint32_t) { return issue(&tm_a, map_b, kb); },
+            [&](int kb) {
+              if (lane == 0) tma_prefetch_l2_2d(&tm_a, kb * kBK, a_row);
+            });
+      } else {
+        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane,
+                                                 [&](int kb, uint32_t) { return issue(&tm_a, map_b, kb); });
+      }
     }
     if (!ok && lane == 0) {
       // Error path: let the copies this warp started land before the CTA exits.
