@@ -206,8 +206,8 @@ struct GemmTraits {
   static_assert(EPI == 4 || EPI == 8, "4 or 8 epilogue warps");
   static_assert(kTmemCols <= 512, "TMEM has 512 columns");
   static_assert(RING == 0 || (RING >= 2 && RING <= kWarpChunks), "a ring has 2 .. kWarpChunks slots");
-  static_assert(!(KIND == KIND_HEAD && BN == 256) || (CG == 2 && RING > 0),
-                "a head work item of two vocabulary tiles runs on a CTA pair with an output ring");
+  static_assert(!(KIND == KIND_HEAD && BN == 256) || RING > 0,
+                "a head work item of two vocabulary tiles writes through an output ring");
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB shared-memory limit");
 };
 
@@ -564,11 +564,16 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
       const int a_row = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM;
       int b_row = n_col0 + static_cast<int>(rank) * ((half ? BN / 2 : BN) / CG);
+      int b_row2 = b_row;  // KIND_HEAD, one CTA: the second vocabulary tile of the item
       if constexpr (head_pairs<KIND, BN>()) {
-        // Each CTA of the pair loads its own vocabulary tile (BN / CG = 128 rows).
+        // A CTA pair: each CTA loads its own vocabulary tile (BN / CG = 128 rows).  One
+        // CTA: both tiles, as two 128-row boxes stacked in the stage.
         int mb, c0, c1;
         head_pair_coords(p, t, mb, c0, c1);
-        if (!half) b_row = rank == 0 ? c0 : c1;
+        if (!half) {
+          b_row = (CG == 1 || rank == 0) ? c0 : c1;
+          b_row2 = c1;
+        }
       }
       // A half-width item loads half of B through the second B map (a box of BN/2/CG rows).
       const CUtensorMap* map_b = half ? &tm_b2 : &tm_b;
@@ -583,6 +588,11 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
               mbar_arrive_expect_tx(&full[stage], stage_bytes);
               tma_load_2d(s_a + stage * Tr::kABytes, ma, &full[stage], kb * kBK, a_row, 0ull);
               tma_load_2d(s_b + stage * Tr::kBBytes, mb, &full[stage], kb * kBK, b_row, pol_b);
+              if constexpr (head_pairs<KIND, BN>()) {
+                if (!half)
+                  tma_load_2d(s_b + stage * Tr::kBBytes + (BN / 2) * kBK * 2, mb, &full[stage], kb * kBK, b_row2,
+                              pol_b);
+              }
             } else {
               // Both CTAs' bytes land on the leader's barrier; only the leader arrives.
               if (leader) mbar_arrive_expect_tx(&full[stage], CG * stage_bytes);
@@ -671,7 +681,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         // its vocabulary tiles times the 128-token halves of its M-block in range.
         unsigned long long weight = (!half || ((t - p.tail_from) & 1) == 0) ? 1ull : 0ull;
         if constexpr (head_pairs<KIND, BN>())
-          weight = (half ? 1ull : 2ull) * (m_blk * Tr::kTileM + kBM < p.M ? 2ull : 1ull);
+          weight = (half ? 1ull : 2ull) * (CG == 2 && m_blk * Tr::kTileM + kBM < p.M ? 2ull : 1ull);
         skipped_steps += weight * static_cast<unsigned long long>(k_steps_total - live_steps);
         issued_steps += weight * static_cast<unsigned long long>(live_steps);
         // A tile without live K-blocks needs no MMA: the epilogue writes the

@@ -112,10 +112,10 @@ def test_sparse_head_module_masks_inactive_tiles():
 @pytest.mark.parametrize("t,d", [(200, 128), (320, 512), (768, 512), (100, 1024)])
 @pytest.mark.parametrize("n_active", [1, 2, 3, 8])
 def test_n_gated_head_pairs_of_vocabulary_tiles(dtype, t, d, n_active):
-    """From d = 512 the dense and N-gated head run two listed vocabulary tiles per CTA
-    pair: odd lists (a lone last tile), unsorted and non-adjacent tiles, token counts
-    that leave a partial 256-token block; stats count per 128-token x 128-column tile,
-    as the single-CTA kernel (d = 128 here) does."""
+    """The dense and N-gated head run two listed vocabulary tiles per work item, on a CTA
+    pair from d = 512 and on one CTA below (d = 128 here): odd lists (a lone last tile),
+    unsorted and non-adjacent tiles, token counts that leave a partial 256-token block;
+    stats count per 128-token x 128-column tile in both forms."""
     from sparsity_spillover_b200 import ops
 
     g = torch.Generator().manual_seed(7 * t + n_active)
