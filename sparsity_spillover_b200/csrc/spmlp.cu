@@ -60,10 +60,11 @@ constexpr int kDownFineBN = 256, kDownFineStages = 4, kDownFineEpiWarps = 4, kDo
 constexpr int kHeadStages = 4, kHeadEpiWarps = 8, kHeadRing = 2;
 // Dense and N-gated head: work items of two vocabulary tiles on a CTA pair (256 x 256).
 constexpr int kHeadPairStages = 5, kHeadPairEpiWarps = 8, kHeadPairRing = 2;
-// Dense and N-gated head below kHeadPairMinD: two vocabulary tiles per item on one CTA
-// (0 = one tile per item, the K-gated kernel's form).  Measured on B200, cfg4 shapes, 5-100 %
-// active tiles: 1.2-1.4x faster than one tile per item at d = 128, 1.1-1.2x faster than the
-// pair kernel at d = 256; the pair kernel wins at d = 512 (its operand stream is half).
+// Head on one CTA with two vocabulary tiles per item (dense and N gate below kHeadPairMinD,
+// the K gate always; 0 = one tile per item).  Measured on B200, cfg4 shapes: 1.2-1.4x faster
+// than one tile per item at d = 128 (N gate, 5-100 % active tiles), 1.6-1.9x for the K gate,
+// 1.1-1.2x faster than the pair kernel at d = 256; the pair kernel wins at d = 512 (its
+// operand stream is half).
 constexpr int kHeadWide = 1, kHeadWideStages = 3, kHeadWideEpiWarps = 8, kHeadWideRing = 2;
 constexpr int kHeadPairMinD = 512;  // d from which the pair kernel is faster
 // Joint consumer: 256 output columns per tile, so that h is read by only d/256
@@ -674,12 +675,12 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
   constexpr int BN = 128;
-  // The K-gated head skips K16 groups dead for its 128 tokens (single CTA, one
-  // vocabulary tile per item).  The dense and N-gated heads run two vocabulary tiles
-  // per item: with d >= kHeadPairMinD on a CTA pair (each CTA loads one tile of
-  // w_vocab, 128 rows), which halves the operand traffic per MMA; below it on one CTA
-  // (both tiles stacked in the stage), where the logit stores bound the head and one
-  // 256-column item halves the epilogue's per-item cost.
+  // Every form runs two vocabulary tiles per work item.  The dense and N-gated heads
+  // with d >= kHeadPairMinD do so on a CTA pair (each CTA loads one tile of w_vocab,
+  // 128 rows), which halves the operand traffic per MMA.  Below it, and for the
+  // K-gated head at any d (it skips K16 groups dead for its 128 tokens, a granule a
+  // pair would double), one CTA loads both tiles stacked in the stage: one 256-column
+  // item halves the epilogue's per-item cost where the logit stores bound the head.
   const bool pairs = gate_axis != SPMLP_HEAD_GATE_K && d >= kHeadPairMinD;
   CUtensorMap ta, tb, tb_half;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
@@ -700,7 +701,7 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   p.stats = reinterpret_cast<unsigned long long*>(stats);
   // Eight epilogue warps (two 32-column chunks each) and a two-slot output ring:
   // the logit stores, not the MMAs, bound the head at d = 128.
-  if (kHeadWide && !pairs && gate_axis != SPMLP_HEAD_GATE_K) {
+  if (kHeadWide && !pairs) {
     constexpr int SW = kHeadWideStages, EW = kHeadWideEpiWarps, RW = kHeadWideRing;
     if (bf16) return launch_gemm<KIND_HEAD, 0, 2 * BN, SW, true, EW, 1, RW>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb);
     return launch_gemm<KIND_HEAD, 0, 2 * BN, SW, false, EW, 1, RW>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb);
