@@ -358,6 +358,23 @@ def head_bench(device, steps=5) -> list[dict]:
             rows.append({"d": d, "active_fraction": frac, "n_gated_us": t_n * 1e6, "dense_us": t_dense * 1e6,
                          "cublas_us": t_cublas * 1e6, "speedup_vs_cublas": t_cublas / t_n,
                          "logit_write_gbs": t_tokens * tiles.numel() * 128 * 2 / t_n / 1e9})
+        if d == 128:
+            # the reference's own head mode: 16x16 corner certificates of the fp32 head input
+            # (runs/068-…/inference/head.cu), dead K16 steps skipped per 128-token block
+            g = torch.Generator(device=device).manual_seed(68)
+            xf = torch.randn(t_tokens, d, generator=g, device=device)
+            for kappa in (0.0, 1.0, 2.0):
+                xh, support = ops.head_prepare(xf, kappa, torch.float16)
+                st = torch.zeros(2, dtype=torch.int64, device=device)
+                ops.head_sparse(xh, w, support=support, logits=logits, stats=st)
+                issued, skipped = st.tolist()
+                t_prep = time_device(lambda: ops.head_prepare(xf, kappa, torch.float16, x_out=xh, support=support),
+                                     steps, device)
+                t_k = time_device(lambda: ops.head_sparse(xh, w, support=support, logits=logits), steps, device)
+                rows.append({"d": d, "mode": "k_gate_corner16x16", "kappa": kappa,
+                             "skipped_k16_fraction": skipped / max(1, issued + skipped),
+                             "prepare_us": t_prep * 1e6, "k_gated_us": t_k * 1e6, "dense_us": t_dense * 1e6,
+                             "cublas_us": t_cublas * 1e6, "speedup_vs_cublas": t_cublas / (t_prep + t_k)})
         del x, w, logits
         torch.cuda.empty_cache()
     return rows
