@@ -2,7 +2,7 @@
 
     python -m sparsity_spillover_b200.profile_case --case mlp  [--tokens 32768] [--iters 3]
     python -m sparsity_spillover_b200.profile_case --case tile [--p 0.1] [--skip fine]
-    python -m sparsity_spillover_b200.profile_case --case head [--d 128] [--frac 0.1]
+    python -m sparsity_spillover_b200.profile_case --case head [--d 128] [--frac 0.1] [--kappa K]
     python -m sparsity_spillover_b200.profile_case --case joint [--tokens 32768]
 
 * ``mlp``  one cfg1 layer (d=512, F=2048, fp16, one-sided gate at 10% density):
@@ -10,7 +10,8 @@
 * ``tile`` cfg2: a tile-structured bf16 h (64x64 tiles live with probability p),
            its bitmap, and the tile-skipping down_sparse (d=512, F=2048) in the
            ``--skip`` mode (coarse: 256-token pair tiles, fine: 128-token tiles).
-* ``head`` cfg4: the N-gated vocabulary head on Zipf-chosen 128-column tiles.
+* ``head`` cfg4: the N-gated vocabulary head on Zipf-chosen 128-column tiles, or with
+           ``--kappa`` the K-gated head (16x16 corner certificates of an fp32 N(0,1) input).
 * ``joint`` the joint consumer on a cfg1 layer: up_gate (identity, then gated) once,
            then the joint kernel ``iters`` times (h at 10% density, z ~ N(0,1)).
 
@@ -34,6 +35,7 @@ def main() -> None:
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--frac", type=float, default=0.1)
     ap.add_argument("--skip", choices=["coarse", "fine"], default="coarse")
+    ap.add_argument("--kappa", type=float, default=None, help="head: K gate with this threshold")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     with torch.inference_mode():
@@ -70,10 +72,16 @@ def main() -> None:
                 ops.down_sparse(h, bits, w, None, skip=args.skip, y=y)
         else:
             x, w = workloads.head_inputs(args.tokens, args.d, seed=4, device=dev)
-            tiles = torch.from_numpy(workloads.zipf_active_tiles(workloads.VOCAB // 128, args.frac, 5)).to(dev)
             logits = torch.empty(args.tokens, workloads.VOCAB, dtype=torch.float16, device=dev)
-            for _ in range(args.iters):
-                ops.head_sparse(x, w, active_tiles=tiles, logits=logits)
+            if args.kappa is not None:
+                xf = torch.randn(args.tokens, args.d, generator=torch.Generator(device=dev).manual_seed(68), device=dev)
+                xh, support = ops.head_prepare(xf, args.kappa, torch.float16)
+                for _ in range(args.iters):
+                    ops.head_sparse(xh, w, support=support, logits=logits)
+            else:
+                tiles = torch.from_numpy(workloads.zipf_active_tiles(workloads.VOCAB // 128, args.frac, 5)).to(dev)
+                for _ in range(args.iters):
+                    ops.head_sparse(x, w, active_tiles=tiles, logits=logits)
         torch.cuda.synchronize(dev)
     print(f"profile_case {args.case}: ok, device status {ops.device_status(0)}")
 
