@@ -294,6 +294,28 @@ __device__ __forceinline__ bool for_each_live_kblock_ahead(const GemmParams& p, 
   return true;
 }
 
+// Whether an M-tile of GROUPS 16-row groups has any live K granule (warp-collective):
+// the answer count_live gives as live_blocks > 0, from one bitmap word per lane
+// (lane i reads word i of the tile's GROUPS x chunks words) instead of GROUPS per lane.
+template <int KIND, int GROUPS>
+__device__ __forceinline__ bool any_live(const GemmParams& p, int m_blk, int lane) {
+  if (!p.skip || p.bits_in == nullptr) return p.K >= kBK;
+  const int row_groups = (p.M + kBitsRows - 1) / kBitsRows;
+  const int granules = k_granules<KIND>(p.K);
+  const int chunks = (granules + 31) / 32;
+  uint32_t any = 0;
+  for (int i = lane; i < GROUPS * chunks; i += 32) {
+    const int r = i % GROUPS, c = i / GROUPS;
+    const int rg = m_blk * GROUPS + r;
+    if (rg < row_groups) {
+      const int valid = granules - 32 * c;  // granule bits of this word that exist
+      const uint32_t mask = valid >= 32 ? 0xffffffffu : ((1u << valid) - 1u);
+      any |= __ldg(p.bits_in + static_cast<size_t>(rg) * p.bits_words + c) & mask;
+    }
+  }
+  return __ballot_sync(0xffffffffu, any != 0) != 0;
+}
+
 // Count of live K-blocks and of live K16 steps of an M-tile (warp-collective).
 template <int KIND, int GROUPS>
 __device__ __forceinline__ void count_live(const GemmParams& p, int m_blk, int lane, int& blocks, int& steps) {
@@ -837,8 +859,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         if constexpr (head_pairs<KIND, BN>()) return ch < 4 ? n_col0 + ch * 32 : n_col1 + (ch - 4) * 32;
         return n_col0 + ch * 32;
       };
-      int live_blocks = 1, live_steps = 0;
-      if constexpr (KIND != KIND_UP) count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
+      int live_blocks = 1;  // > 0: the MMA warp wrote this item's accumulator
+      if constexpr (KIND != KIND_UP) live_blocks = any_live<KIND, kGroups>(p, m_blk, lane) ? 1 : 0;
       const int row0 = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
