@@ -294,8 +294,8 @@ __device__ __forceinline__ bool for_each_live_kblock_ahead(const GemmParams& p, 
   return true;
 }
 
-// Whether an M-tile of GROUPS 16-row groups has any live K granule (warp-collective):
-// the answer count_live gives as live_blocks > 0, from one bitmap word per lane
+// Whether an M-tile of GROUPS 16-row groups has any live K granule (warp-collective),
+// i.e. whether for_each_live_kblock would visit any K-block: one bitmap word per lane
 // (lane i reads word i of the tile's GROUPS x chunks words) instead of GROUPS per lane.
 template <int KIND, int GROUPS>
 __device__ __forceinline__ bool any_live(const GemmParams& p, int m_blk, int lane) {
@@ -314,18 +314,6 @@ __device__ __forceinline__ bool any_live(const GemmParams& p, int m_blk, int lan
     }
   }
   return __ballot_sync(0xffffffffu, any != 0) != 0;
-}
-
-// Count of live K-blocks and of live K16 steps of an M-tile (warp-collective).
-template <int KIND, int GROUPS>
-__device__ __forceinline__ void count_live(const GemmParams& p, int m_blk, int lane, int& blocks, int& steps) {
-  blocks = 0;
-  steps = 0;
-  for_each_live_kblock<KIND, GROUPS>(p, m_blk, lane, [&](int, uint32_t k16) {
-    ++blocks;
-    steps += __popc(k16);
-    return true;
-  });
 }
 
 template <int KIND, int BN>
@@ -696,19 +684,19 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         int m_blk, n_col0;
         const bool half = work_coords<KIND, BN>(p, t, m_blk, n_col0);
         const uint32_t idesc = half ? idesc_half : idesc_full;
-        int live_blocks, live_steps;
-        count_live<KIND, kGroups>(p, m_blk, lane, live_blocks, live_steps);
         // Counted per whole tile: a split tile's second half adds nothing.  A head
         // item counts per 128-token x 128-column tile, as the single-CTA head does:
         // its vocabulary tiles times the 128-token halves of its M-block in range.
         unsigned long long weight = (!half || ((t - p.tail_from) & 1) == 0) ? 1ull : 0ull;
         if constexpr (head_pairs<KIND, BN>())
           weight = (half ? 1ull : 2ull) * (CG == 2 && m_blk * Tr::kTileM + kBM < p.M ? 2ull : 1ull);
-        skipped_steps += weight * static_cast<unsigned long long>(k_steps_total - live_steps);
-        issued_steps += weight * static_cast<unsigned long long>(live_steps);
         // A tile without live K-blocks needs no MMA: the epilogue writes the
-        // zero-accumulator result itself (the joint always has its z branch).
-        if (KIND != KIND_JOINT && live_blocks == 0) continue;
+        // zero-accumulator result itself (the joint always has its z branch).  The live
+        // K16 steps of the others are counted while their MMAs are issued below.
+        if (KIND != KIND_JOINT && !any_live<KIND, kGroups>(p, m_blk, lane)) {
+          skipped_steps += weight * static_cast<unsigned long long>(k_steps_total);
+          continue;
+        }
         if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
@@ -749,9 +737,14 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           if (!ok) break;
         }
         uint32_t accumulate = 0;
-        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane,
-                                                 [&](int, uint32_t k16) { return mma_stage(d_tmem, k16, accumulate); });
+        int live_steps = 0;
+        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int, uint32_t k16) {
+          live_steps += __popc(k16);
+          return mma_stage(d_tmem, k16, accumulate);
+        });
         if (!ok) break;
+        skipped_steps += weight * static_cast<unsigned long long>(k_steps_total - live_steps);
+        issued_steps += weight * static_cast<unsigned long long>(live_steps);
         if (lane == 0) umma_commit<CG>(&acc_full[acc]);
         __syncwarp();
         if (++acc == Tr::kAccBufs) {
