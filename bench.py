@@ -1,6 +1,6 @@
 """Benchmark of the B200 sparse gated MLP (driver contract: one JSON line on rank 0).
 
-Workload: Pythia-70M MLP, 6 stacked layers, d=512, F=2048,
+Workload (the headline configuration): Pythia-70M MLP, 6 stacked layers, d=512, F=2048,
 T=32768 tokens per GPU, fp16, one-sided threshold gate at 10% element density
 (kappa calibrated per layer by the kthvalue rule).  Layers are chained through
 the parallel residual, x_{l+1} = round(x_l + MLP_l(x_l)), which the down-projection
@@ -501,11 +501,11 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
     # The fused split in both forms: partials stored into peers' receive buffers, and the
     # reduction + broadcast through NVSwitch multicast (when the system offers it).
     fused_peer = sdist.FusedDffSplit(split, t_rank * world, multicast=False)
-    runs = [("dff_split", run_split), ("dff_split_fused_peer", lambda: fused_peer.forward(x_all))]
+    runs = [("dff_split", run_split), ("dff_split_fused_peer", lambda: fused_peer.forward(x_all, check=False))]
     fused_mc = None
     if sdist.multicast_available(device):
         fused_mc = sdist.FusedDffSplit(split, t_rank * world, multicast=True)
-        runs.append(("dff_split_fused_multicast", lambda: fused_mc.forward(x_all)))
+        runs.append(("dff_split_fused_multicast", lambda: fused_mc.forward(x_all, check=False)))
     runs.append(("token_sharded", run_tokens))
     out = {}
     for name, fn in runs:
@@ -521,6 +521,193 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
     out["dff_split_fused_form"] = chosen
     out.update(layers=layers, tokens_per_rank=t_rank, world=world,
                collective_bytes_per_layer=2 * (world - 1) * t_rank * cfg.d * 2)
+    out["parity"] = dff_split_parity(runs, run_tokens, world, device)
+    return out
+
+
+def dff_split_parity(runs, run_tokens, world: int, device) -> dict:
+    """Every d_ff-split form's output block on this rank against the single-GPU forward of
+    the same tokens and layers (token-local, so this rank's rows alone): max relative error
+    max|y - y_ref| / max|y_ref|, the max over ranks, and the device status word."""
+    import torch
+    import torch.distributed as dist
+
+    from sparsity_spillover_b200 import ops
+
+    ref = run_tokens().clone()
+    ref64 = ref.double()
+    denom = float(ref64.abs().max())
+    errs = []
+    names = [name for name, _ in runs if name != "token_sharded"]
+    for name, fn in runs:
+        if name == "token_sharded":
+            continue
+        y = fn()
+        torch.cuda.synchronize(device)
+        errs.append(float((y.double() - ref64).abs().max()) / max(denom, 1e-30))
+    status = ops.device_status(device.index)
+    vec = torch.tensor(errs + [float(status)], dtype=torch.float64, device=device)
+    dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+    vals = vec.cpu().tolist()
+    res = {f"{n}_max_rel_err": vals[i] for i, n in enumerate(names)}
+    res["reference"] = "ops.mlp_forward chain of the same layers over this rank's tokens on one GPU (fp16)"
+    res["tolerance"] = 2e-3
+    res["ok"] = all(v <= 2e-3 for v in vals[:-1]) and vals[-1] == 0
+    res["device_status_max"] = int(vals[-1])
+    return res
+
+
+def cfg0_block(device, reps: int = 64, steps: int = 10) -> dict:
+    """cfg0, the Pythia-14M MLP block (T=4096, d=128, F=512, one-sided gate at 10 % density),
+    on the exact seeded tensors of the reference's CPU case: on the GPU in fp16 as one CUDA
+    graph of `reps` back-to-back forwards (the shape is HBM- and launch-bound; the graph
+    amortises launches), against stock PyTorch captured the same way; and the reference's
+    CPU path (the fp32 oracle restatement) on the same tensors with every host thread."""
+    import torch
+
+    from oracle import gates as og
+    from oracle import mlp as omlp
+    from sparsity_spillover_b200 import ops, workloads
+
+    cfg = workloads.CONFIGS["cfg0"]
+    L = workloads.make_weights(cfg, "cpu", dtype=torch.float32)[0]
+    x32 = workloads.make_input(cfg, "cpu", dtype=torch.float32)
+    t, d, f = cfg.tokens, cfg.d, cfg.F
+    # CPU arm: fp32, the reference's kthvalue threshold of z
+    with torch.inference_mode():
+        z32 = omlp.linear(x32, L.w_in, L.b_in)
+        k32 = max(0.0, og.kthvalue_threshold(z32, cfg.density))
+        omlp.mlp_forward_fp32(x32, L.w_in, L.b_in, L.w_out, L.b_out, og.ONE_SIDED, k32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 5.0 or n < 3:
+            omlp.mlp_forward_fp32(x32, L.w_in, L.b_in, L.w_out, L.b_out, og.ONE_SIDED, k32)
+            n += 1
+        cpu_s = (time.perf_counter() - t0) / n
+    # GPU arm: the same tensors in fp16
+    x = x32.half().to(device)
+    w_in, b_in, w_out, b_out = (v.half().to(device) for v in (L.w_in, L.b_in, L.w_out, L.b_out))
+    z = torch.empty(t, f, dtype=torch.float16, device=device)
+    ops.up_gate(x, w_in, b_in, {"operator": "identity"}, z_out=z)
+    gate = {"operator": "one_sided_threshold", "kappa": workloads.quantile_threshold(z, cfg.density)}
+    h = torch.empty(t, f, dtype=torch.float16, device=device)
+    bits = torch.empty(ops.tile_bits_size(t, f), dtype=torch.int32, device=device)
+    y = torch.empty(t, d, dtype=torch.float16, device=device)
+
+    def ours():
+        for _ in range(reps):
+            ops.mlp_forward(x, w_in, b_in, w_out, b_out, gate, h=h, bits=bits, y=y)
+
+    def stock():
+        for _ in range(reps):
+            zz = torch.nn.functional.linear(x, w_in, b_in)
+            torch.nn.functional.linear(zz.masked_fill(zz < gate["kappa"], 0.0), w_out, b_out)
+
+    t_ours = time_device(graph_of(ours, device).replay, steps, device) / reps
+    t_stock = time_device(graph_of(stock, device).replay, steps, device) / reps
+    density = float((h != 0).float().mean())
+    nbytes = 2.0 * (t * d + f * d + f + 2 * t * f + f * d + d + t * d) + t * f / 8192.0
+    return {"tokens": t, "d": d, "F": f, "density_measured": round(density, 4),
+            "gpu_us_per_forward": t_ours * 1e6, "gpu_tokens_per_s": t / t_ours,
+            "stock_pytorch_us_per_forward": t_stock * 1e6, "speedup_vs_stock": t_stock / t_ours,
+            "gpu_algorithmic_gbs": nbytes / t_ours / 1e9,
+            "gpu_execution": f"CUDA graph of {reps} forwards (up_gate + down_sparse), fp16",
+            "cpu_tokens_per_s": t / cpu_s, "cpu_ms_per_forward": cpu_s * 1e3,
+            "cpu_threads": torch.get_num_threads(), "cpu_kind": "port (fp32 oracle restatement)",
+            "gpu_over_cpu": cpu_s / t_ours}
+
+
+def host_link(device, nbytes: int, world: int, reps: int = 5) -> dict:
+    """Copy-only probe of this rank's host link with the e2e step's byte count: pinned host ->
+    device, device -> pinned host, and both at once on two streams (GB/s, each the max time over
+    ranks, all ranks copying at the same time)."""
+    import torch
+
+    host_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    host_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev_a = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev_b = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def timed(fn) -> float:
+        fn()
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize(device)
+        dt = (time.perf_counter() - t0) / reps
+        return max_over_ranks(dt, world, device)
+
+    def h2d():
+        with torch.cuda.stream(s1):
+            dev_a.copy_(host_in, non_blocking=True)
+
+    def d2h():
+        with torch.cuda.stream(s2):
+            host_out.copy_(dev_b, non_blocking=True)
+
+    def both():
+        h2d()
+        d2h()
+
+    t_in, t_out, t_both = timed(h2d), timed(d2h), timed(both)
+    return {"bytes_each_way": nbytes, "h2d_gbs": nbytes / t_in / 1e9, "d2h_gbs": nbytes / t_out / 1e9,
+            "concurrent_gbs_each_way": nbytes / t_both / 1e9, "concurrent_ms": t_both * 1e3,
+            "timing": "host clock around synchronised copies, max over ranks"}
+
+
+def summarize(line: dict) -> dict:
+    """The per-config figures in a few short keys (kept at the end of the JSON line)."""
+    out: dict = {}
+
+    def r(v, n=3):
+        return None if v is None else round(float(v), n)
+
+    sweep = line.get("density_sweep")
+    if isinstance(sweep, list):
+        out["density_sweep_mtok_s"] = {str(x["density_target"]): r(x["tokens_per_s"] / 1e6, 2) for x in sweep}
+        out["density_sweep_speedup_vs_rho1"] = {str(x["density_target"]): r(x["speedup_vs_ours_at_100pct"])
+                                                for x in sweep}
+        out["density_sweep_speedup_vs_stock"] = {str(x["density_target"]): r(x["speedup_vs_dense_pytorch"])
+                                                 for x in sweep}
+    c2 = line.get("tile_structured_cfg2")
+    if isinstance(c2, list):
+        out["cfg2_us"] = {f"d{x['d']}_p{x['p']}": [r(x["down_fine_us"], 1), r(x["down_coarse_us"], 1),
+                                                   r(x["cublas_us"], 1), r(x["skipped_k16_fraction_fine"])]
+                          for x in c2}
+        out["cfg2_us_fields"] = ["fine", "coarse", "cublas", "skipped_k16_fraction_fine"]
+    c3 = line.get("pythia410m_cfg3")
+    if isinstance(c3, dict) and "tokens_per_s" in c3:
+        out["cfg3_mtok_s"] = r(c3["tokens_per_s"] / 1e6)
+        out["cfg3_executed_tflops"] = r(c3["executed_tflops"], 1)
+        out["cfg3_speedup_vs_stock"] = r(c3["speedup_vs_dense_pytorch"])
+    j = line.get("joint_cfg1")
+    if isinstance(j, dict) and "fused_us" in j:
+        out["joint_us"] = {"fused": r(j["fused_us"], 1), "stock": r(j["stock_pytorch_us"], 1),
+                           "speedup": r(j["speedup_vs_stock"])}
+    hd = line.get("vocab_head_cfg4")
+    if isinstance(hd, list):
+        out["head_speedup_vs_cublas"] = {
+            (f"d{x['d']}_k{x['kappa']}" if x.get("mode") else f"d{x['d']}_n{x['active_fraction']}"):
+                r(x["speedup_vs_cublas"]) for x in hd}
+        dense = {f"d{x['d']}": r(x["cublas_us"] / x["dense_us"]) for x in hd if "dense_us" in x}
+        out["head_dense_speedup_vs_cublas"] = dense
+    c0 = line.get("cfg0_block")
+    if isinstance(c0, dict) and "gpu_tokens_per_s" in c0:
+        out["cfg0"] = {"gpu_mtok_s": r(c0["gpu_tokens_per_s"] / 1e6, 1), "cpu_ktok_s": r(c0["cpu_tokens_per_s"] / 1e3, 1),
+                       "speedup_vs_stock": r(c0["speedup_vs_stock"])}
+    hl = line.get("host_link")
+    if isinstance(hl, dict) and "h2d_gbs" in hl:
+        out["host_link_gbs"] = [r(hl["h2d_gbs"], 1), r(hl["d2h_gbs"], 1), r(hl["concurrent_gbs_each_way"], 1)]
+    ds = line.get("dff_split_cfg3")
+    if isinstance(ds, dict) and "parity" in ds:
+        out["dff_split_mtok_s"] = {k[len("dff_split"):].strip("_") or "nccl": r(v / 1e6, 2)
+                                   for k, v in ds.items() if k.endswith("tokens_per_s")}
+        out["dff_split_parity"] = {k: v for k, v in ds["parity"].items() if k != "reference"}
+    out["value_mtok_s"] = r(line["value"] / 1e6, 2)
+    out["e2e_mtok_s"] = r(line["e2e"]["value"] / 1e6, 2)
+    out["roofline_frac"] = r(line["roofline"]["frac"])
     return out
 
 
@@ -673,6 +860,7 @@ def run_ours(args):
         stop_e.record()
         torch.cuda.synchronize(device)
         t_e2e = max_over_ranks(start_e.elapsed_time(stop_e) / 1e3 / args.steps, world, device)
+        link = _extra(host_link, device, t * d * 2, world)
 
         # ---- the same forward as stock PyTorch on CUDA (cuBLAS + masked_fill), for the ratio
         # (captured as a CUDA graph too, so both sides run without host launch gaps)
@@ -738,6 +926,7 @@ def run_ours(args):
                      "roofline: eager steps with per-kernel CUDA events",
         "clocks": clocks,
         "device_status": status,
+        "host_link": link,
     }
     if world > 1 and not args.no_extras:
         line["dff_split_cfg3"] = _extra(dff_split_measure, device, world, rank)
@@ -752,6 +941,7 @@ def run_ours(args):
             line["vocab_head_cfg4"] = _extra(head_bench, device)
             line["joint_cfg1"] = _extra(joint_cfg1, device)
             line["layernorm_fold_cfg1"] = _extra(layernorm_fold_cfg1, device)
+            line["cfg0_block"] = _extra(cfg0_block, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
     if world > 1:
@@ -760,6 +950,7 @@ def run_ours(args):
         dist.barrier(device_ids=[device.index])
         dist.destroy_process_group()
     if rank == 0:
+        line["summary"] = summarize(line)  # last key: survives a truncated tail of the output
         print(json.dumps(line), flush=True)
 
 

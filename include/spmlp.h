@@ -23,7 +23,11 @@
  *   - No entry point allocates device memory except where stated.
  *   - The kernels never trap: a device-side wait that does not finish within
  *     2 s records a code in the per-device status word (spmlp_device_status)
- *     and the kernel returns.
+ *     and the kernel returns early, leaving its outputs incomplete.  The code
+ *     stays set until spmlp_clear_device_status; kernels launched afterwards
+ *     run normally (each compares the word against the value it found at
+ *     launch).  A caller that must know whether a result is good reads the
+ *     status word after the work it depends on.
  */
 #ifndef SPMLP_H_
 #define SPMLP_H_
@@ -106,8 +110,12 @@ int spmlp_tile_bits_from_h(const void* h, uint32_t* tile_bits, int64_t T, int F,
  *   x [T,d], w_in [F,d], b_in [F] (nullable) -> h [T,F], tile_bits (zeroed
  *   here, then filled), z_out [T,F] (nullable: the pre-gate z, for checks).
  *   kappa must already be rounded to the activation dtype (runs/063-2026-10-07-pythia14m-tile-specialized-kernel/kernel.py:17-19).
- *   seq_len: tokens per sequence for SPMLP_GATE_CORNER (blocks restart per
- *   sequence; seq_len % 8 == 0 or seq_len == T), ignored otherwise.
+ *   seq_len: tokens per sequence for SPMLP_GATE_CORNER (T a multiple of it;
+ *   8-token blocks restart at each sequence, and a sequence whose length is not
+ *   a multiple of 8 ends with a shorter block decided by its own first row, as
+ *   runs/063-2026-10-07-pythia14m-tile-specialized-kernel/tile_gate.py:25-28
+ *   allows; with several such sequences the gate runs as a second in-place pass
+ *   over h), ignored otherwise.
  *   Requires d % 64 == 0, F % 64 == 0, 1 <= T < 2^31. */
 int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, uint32_t* tile_bits,
                   void* z_out, int64_t T, int d, int F, int dtype, int gate_op, float kappa,
@@ -185,8 +193,9 @@ int spmlp_reduce_broadcast_multicast(const void* mc_part, void* mc_x, const void
  * rank j's int64 flag array, [world]) after a system-scope fence, then waits until
  * local_flags[j] >= epoch for every j.  epoch must grow from call to call (flags
  * start at 0).  Each wait gives up after about 2 s with SPMLP_STATUS_TIMEOUT_PEER
- * in the status word; nothing faults.  One rank per GPU: ranks sharing a GPU can
- * wait on each other forever, so that is not supported. */
+ * in the status word; nothing faults.  One rank per GPU: two ranks sharing a
+ * GPU are not guaranteed to run at the same time, so one would wait out the 2 s
+ * limit and give up; that is not supported. */
 int spmlp_peer_barrier(long long* const* peer_slots, const long long* local_flags, int world, long long epoch,
                        void* stream);
 
@@ -294,8 +303,10 @@ int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, 
                     float value, void* stream);
 
 /* Status word of `device` written by kernels that gave up on a bounded wait
- * (0 = none; the first code recorded stays until cleared; once it is set, later
- * waits give up at once so a failed launch unwinds quickly).  Reading
+ * (0 = none; otherwise the code of the most recent wait that gave up, which
+ * stays until cleared).  Within one launch, the first wait that gives up makes
+ * the launch's other waits give up at once, so a failed launch unwinds quickly;
+ * later launches are not affected by a code that is already set.  Reading
  * synchronises that device.  clear resets it to 0. */
 #define SPMLP_STATUS_OK 0
 #define SPMLP_STATUS_TIMEOUT_PRODUCER 1 /* TMA warp: no free pipeline stage          */
@@ -311,7 +322,7 @@ int spmlp_clear_device_status(int device);
  * waits, with the bounded wait every kernel here uses, on a barrier that nothing
  * completes.  After about 2 s it gives up, records SPMLP_STATUS_TIMEOUT_PROBE in
  * the status word and returns; the context stays usable.  Nothing faults or
- * traps.  Clear the status word first: a set word makes the wait give up at once. */
+ * traps.  It waits the full 2 s whether or not the status word is already set. */
 int spmlp_selftest_wait(void* stream);
 
 /* Message of the last failed call on this thread ("" if none). */

@@ -112,4 +112,57 @@ __global__ void __launch_bounds__(256) gate_bits_kernel(const uint16_t* x, uint1
   }
 }
 
+// The corner-tile gate (8-token x 16-feature tiles, kept iff the tile's top-left z >
+// kappa) applied in place to z [T, F], with the 16x64 tile bitmap of the result.
+// Token blocks restart at every sequence start (row multiple of seq_len), so with
+// seq_len % 8 != 0 a block's corner row can lie in another up-projection tile, where
+// the fused epilogue cannot see it; this pass serves that case after an ungated up
+// projection.  The last block of a sequence may be shorter than 8 tokens and is
+// decided by its own first row, as in the reference gate.  In place is safe: a
+// corner that is rejected (z <= kappa, or NaN) may be zeroed by its own thread while
+// others read it, and 0 > kappa is false for every kappa >= 0, so every reader
+// reaches the same decision.  Same grid as tile_bits_kernel.
+template <bool BF16>
+__global__ void __launch_bounds__(256) corner_gate_kernel(uint16_t* z, uint32_t* __restrict__ bits, int T, int F,
+                                                          int words, int seq_len, float kappa) {
+  using D = DType<BF16>;
+  extern __shared__ uint32_t s_words[];
+  const int rg = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) s_words[w] = 0u;
+  __syncthreads();
+  const int tiles = F / 64;
+  const int row = rg * 16 + (lane >> 1);
+  int corner_row = row;
+  if (row < T) {
+    const int s0 = (row / seq_len) * seq_len;
+    corner_row = s0 + ((row - s0) / 8) * 8;
+  }
+  for (int g = warp; g < tiles; g += nwarps) {
+    uint32_t acc = 0;
+    if (row < T) {
+      const int col = g * 64 + (lane & 1) * 32;  // two 16-feature tiles per lane
+      const volatile uint16_t* cz = z + static_cast<size_t>(corner_row) * F + col;
+      const uint32_t keep0 = D::to_float(cz[0]) > kappa ? 0xffffffffu : 0u;
+      const uint32_t keep1 = D::to_float(cz[16]) > kappa ? 0xffffffffu : 0u;
+      uint4* p = reinterpret_cast<uint4*>(z + static_cast<size_t>(row) * F + col);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t keep = i < 2 ? keep0 : keep1;
+        uint4 v = p[i];
+        v.x &= keep;
+        v.y &= keep;
+        v.z &= keep;
+        v.w &= keep;
+        p[i] = v;
+        acc |= (v.x | v.y | v.z | v.w) & 0x7fff7fffu;
+      }
+    }
+    if (__any_sync(0xffffffffu, acc != 0) && lane == 0) atomicOr(&s_words[g >> 5], 1u << (g & 31));
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
+}
+
 }  // namespace spmlp

@@ -132,6 +132,7 @@ __global__ void peer_barrier_kernel(PeerFlags peers, const long long* local, int
                                     int* status) {
   const int j = threadIdx.x;
   if (j >= world) return;
+  const int base = status_base(status);  // errors of earlier launches are not this barrier's
   __threadfence_system();
   asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(peers.dst[j]), "l"(epoch) : "memory");
   const uint64_t start = global_timer_ns();
@@ -139,9 +140,9 @@ __global__ void peer_barrier_kernel(PeerFlags peers, const long long* local, int
     long long seen;
     asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(seen) : "l"(local + j) : "memory");
     if (seen >= epoch) break;
-    if (*reinterpret_cast<volatile int*>(status) != kDevOk) break;  // another wait already failed
+    if (status_changed(status, base)) break;  // another wait of this barrier already failed
     if (global_timer_ns() - start > SPMLP_WAIT_NS) {
-      atomicCAS(status, kDevOk, kDevTimeoutPeer);
+      status_record(status, base, kDevTimeoutPeer);
       break;
     }
     __nanosleep(100);

@@ -414,8 +414,9 @@ struct UpEpilogue {
     } else if constexpr (GATE == GATE_CORNER) {
       // Tiles are 8 tokens x 16 features; the corner row of this thread's
       // block lives in lane (lane & ~7) of the same warp because blocks and
-      // warp row-quarters are both 8-aligned (the host enforces seq_len % 8
-      // == 0 or a single sequence).  Columns 0 and 16 of the chunk are corners.
+      // warp row-quarters are both 8-aligned (the host runs this epilogue only
+      // for seq_len % 8 == 0 or a single sequence, and a separate pass otherwise).
+      // Columns 0 and 16 of the chunk are corners.
       const int src = lane & ~7;
       const uint32_t c0 = __shfl_sync(0xffffffffu, z[0], src);
       const uint32_t c1 = __shfl_sync(0xffffffffu, z[8], src);
@@ -561,6 +562,8 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
   // nothing below reads global memory before that kernel has completed.
   grid_dependency_wait();
   grid_launch_dependents();
+  // Status word as this launch found it: errors of earlier launches are not this one's.
+  const int st0 = status_base(p.status);
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
@@ -592,7 +595,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       auto issue = [&](const CUtensorMap* ma, const CUtensorMap* mb, int kb) -> bool {
         bool good = true;
         if (lane == 0) {
-          good = mbar_wait(&empty[stage], phase ^ 1u, p.status, kDevTimeoutProducer);
+          good = mbar_wait(&empty[stage], phase ^ 1u, p.status, st0, kDevTimeoutProducer);
           if (good) {
             if constexpr (CG == 1) {
               mbar_arrive_expect_tx(&full[stage], stage_bytes);
@@ -656,7 +659,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           const uint64_t start = global_timer_ns();
           while (!mbar_try_wait(&full[s], ph)) {
             if (global_timer_ns() - start > SPMLP_WAIT_NS) {
-              atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
+              status_record(p.status, st0, kDevTimeoutDrain);
               break;
             }
           }
@@ -697,7 +700,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           skipped_steps += weight * static_cast<unsigned long long>(k_steps_total);
           continue;
         }
-        if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kDevTimeoutMma);
+        if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, st0, kDevTimeoutMma);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         tc_fence_after();
@@ -706,7 +709,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         auto mma_stage = [&](uint32_t d, uint32_t k16, uint32_t& accumulate) -> bool {
           bool good = true;
           if (lane == 0) {
-            good = mbar_wait(&full[stage], phase, p.status, kDevTimeoutMma);
+            good = mbar_wait(&full[stage], phase, p.status, st0, kDevTimeoutMma);
             if (good) {
               tc_fence_after();
               const uint64_t a_desc = sw128_kmajor_desc(smem_u32(s_a + stage * Tr::kABytes));
@@ -758,7 +761,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         const uint64_t start = global_timer_ns();
         while (!mbar_try_wait(drain, 0)) {
           if (global_timer_ns() - start > SPMLP_WAIT_NS) {
-            atomicCAS(p.status, kDevOk, kDevTimeoutDrain);
+            status_record(p.status, st0, kDevTimeoutDrain);
             break;
           }
         }
@@ -923,12 +926,12 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
 
       if (has_acc) {
         // Every lane observes the barrier itself before reading TMEM.
-        const bool good = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, p.status, kDevTimeoutEpilogue));
+        const bool good = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, p.status, st0, kDevTimeoutEpilogue));
         if (!good) break;
         tc_fence_after();
       }
       if (!kRing && with_res && row0 < p.M) {
-        const bool good = __all_sync(0xffffffffu, mbar_wait(&res_full[ew], res_phase, p.status, kDevTimeoutEpilogue));
+        const bool good = __all_sync(0xffffffffu, mbar_wait(&res_full[ew], res_phase, p.status, st0, kDevTimeoutEpilogue));
         res_phase ^= 1u;
         if (!good) break;
       }

@@ -2,7 +2,7 @@
 // mbarriers, TMA tile loads, tcgen05 MMA / TMEM allocation / TMEM loads.
 //
 // Every wait in this file is bounded: a barrier that does not complete within
-// SPMLP_WAIT_NS nanoseconds (or whose CTA already saw an error) makes the wait
+// SPMLP_WAIT_NS nanoseconds (or whose launch already saw an error) makes the wait
 // return false, records an error code in the library status word and lets the
 // caller unwind.  No wait spins forever and nothing here traps.
 #pragma once
@@ -68,19 +68,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// The status word holds the code of the most recent wait that gave up (low 8 bits)
+// above a count of such events (bits 8..).  A kernel reads it once when it starts
+// (`base`); its own roles then compare against that value, so an error recorded by
+// an earlier launch neither stops this launch nor hides a new error of its own.
+__device__ __forceinline__ int status_base(const int* status) {
+  return *reinterpret_cast<const volatile int*>(status);
+}
+__device__ __forceinline__ bool status_changed(const int* status, int base) {
+  return *reinterpret_cast<const volatile int*>(status) != base;
+}
+// Record `code` unless another role of this launch already recorded an error.
+__device__ __forceinline__ void status_record(int* status, int base, int code) {
+  atomicCAS(status, base, (((base >> 8) + 1) << 8) | code);
+}
+
 // Wait for the phase with the given parity to complete.  Returns false (and
 // records `code` in *status) when the deadline passes or when another role of
 // this launch already recorded an error; the caller must then unwind.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int base, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(status) != kDevOk) return false;
+    if (status_changed(status, base)) return false;
     if (global_timer_ns() - start > SPMLP_WAIT_NS) {
-      atomicCAS(status, kDevOk, code);
+      status_record(status, base, code);
       return false;
     }
   }

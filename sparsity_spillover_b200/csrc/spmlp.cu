@@ -77,20 +77,44 @@ constexpr int kJointFineStages = 4, kJointFineEpiWarps = 4;
 struct DeviceInfo {
   int sm_count = 0;
   int* status = nullptr;
+  void* ctx = nullptr;  // the context the cached addresses belong to
   bool ok = false;
 };
 
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[kMaxDevices];
 
+// The calling thread's current CUDA context (driver handle), or null.  Device
+// addresses of this module's __device__ variables belong to one context: after a
+// cudaDeviceReset the runtime loads the module again into a new primary context,
+// and addresses cached for the old one are stale.
+void* current_context() {
+  typedef int (*CtxGetCurrentFn)(void**);
+  static CtxGetCurrentFn fn = []() -> CtxGetCurrentFn {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(ptr);
+  }();
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
 int current_device_info(DeviceInfo** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(SPMLP_EDEVICE, "device index %d out of range", dev);
+  // Null until the runtime has made the device's primary context current on this
+  // thread; the symbol lookup below does that, so the entry is then refreshed once.
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_dev_mutex);
   DeviceInfo& info = g_dev[dev];
-  if (!info.ok) {
+  if (!info.ok || ctx == nullptr || info.ctx != ctx) {
+    info.ok = false;
     int major = 0, minor = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -102,6 +126,7 @@ int current_device_info(DeviceInfo** out) {
     e = cudaGetSymbolAddress(&addr, g_device_status);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status word)");
     info.status = static_cast<int*>(addr);
+    info.ctx = current_context();
     info.ok = true;
   }
   *out = &info;
@@ -281,8 +306,6 @@ int check_gate(int gate_op, float kappa, int64_t T, int64_t seq_len) {
   if (gate_op == SPMLP_GATE_CORNER) {
     if (seq_len <= 0) return fail(SPMLP_EINVAL, "corner gate needs seq_len > 0");
     if (T % seq_len != 0) return fail(SPMLP_ESHAPE, "T=%lld is not a multiple of seq_len=%lld", (long long)T, (long long)seq_len);
-    if (seq_len != T && seq_len % 8 != 0)
-      return fail(SPMLP_ESHAPE, "corner gate with several sequences needs seq_len %% 8 == 0");
   }
   return 0;
 }
@@ -358,7 +381,24 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   p.gate_op = gate_op;
   p.kappa = kappa;
   p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : T);
-  return launch_up<BN>(ta, tb, tc, p, gate_op, bf16, stream, dev);
+  // Corner gate over several sequences whose length is not a multiple of 8: a token
+  // block's corner row may belong to another tile, so the up projection writes the
+  // ungated z and corner_gate_kernel gates it in place and rebuilds the bitmap.
+  const bool corner_pass = gate_op == SPMLP_GATE_CORNER && seq_len != T && seq_len % 8 != 0;
+  rc = launch_up<BN>(ta, tb, tc, p, corner_pass ? SPMLP_GATE_IDENTITY : gate_op, bf16, stream, dev);
+  if (rc || !corner_pass) return rc;
+  const int groups = static_cast<int>((T + kBitsRows - 1) / kBitsRows);
+  const size_t smem = static_cast<size_t>(words) * 4;
+  uint16_t* hz = static_cast<uint16_t*>(h);
+  if (bf16)
+    corner_gate_kernel<true><<<groups, 256, smem, stream>>>(hz, bits, static_cast<int>(T), F, words,
+                                                            static_cast<int>(seq_len), kappa);
+  else
+    corner_gate_kernel<false><<<groups, 256, smem, stream>>>(hz, bits, static_cast<int>(T), F, words,
+                                                             static_cast<int>(seq_len), kappa);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "corner_gate_kernel launch");
+  return 0;
 }
 
 // slots != nullptr: the d_ff split's scattering mode (see GemmParams::scatter_out);
@@ -491,7 +531,7 @@ __global__ void wait_probe_kernel(int* status) {
     fence_barrier_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, status, kDevTimeoutProbe);
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, status, status_base(status), kDevTimeoutProbe);
 }
 
 int row_stats_impl(const void* x, float* mean, float* rstd, int64_t T, int d, int dtype, float eps,
@@ -755,21 +795,26 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[64] = {};
+void* g_noalloc_ctx[64] = {};
 
 // Device address of g_noalloc_scratch on the current device.  The host-side
 // symbol is only a stand-in, never a device address; the real address is looked
-// up once per device (cudaGetSymbolAddress, with that device current) and cached.
+// up (cudaGetSymbolAddress, with that device current) once per device and
+// context, and looked up again when the context changes (after a device reset
+// the runtime loads this module again, at a new address).
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(SPMLP_EDEVICE, "device index %d out of range", dev);
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
     g_noalloc_ptr[dev] = ptr;
+    g_noalloc_ctx[dev] = current_context();
   }
   *out = g_noalloc_ptr[dev];
   return 0;
@@ -1071,7 +1116,7 @@ int spmlp_device_status(int device, int* status_out) {
   e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
   cudaSetDevice(prev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status word)");
-  *status_out = v;
+  *status_out = v & 0xff;  // the code; the bits above count the events
   return 0;
 }
 

@@ -267,9 +267,15 @@ class FusedDffSplit:
         self.epoch += 1
         ops.peer_barrier(self.flag_slots, self.flags, self.epoch)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, *, check: bool = True) -> torch.Tensor:
         """x [T, d] (the same on every rank) -> this rank's [T/w, d] block of the last
-        layer's output; the whole output is in ``self.x`` on every rank."""
+        layer's output; the whole output is in ``self.x`` on every rank.
+
+        A peer barrier that gives up (a peer did not signal within about 2 s: a slow,
+        stuck or missing rank) lets the reduction run on partials that may be
+        incomplete.  With ``check`` (default) the call waits for its kernels and raises
+        ``PeerTimeoutError`` when the device status word reports such a failure; pass
+        ``check=False`` inside timed loops and read ``ops.device_status`` afterwards."""
         from . import ops
 
         if tuple(x.shape) != (self.tokens, self.d):
@@ -290,4 +296,20 @@ class FusedDffSplit:
                 self._barrier()
                 ops.reduce_broadcast(self.recv, layer.b_out, mine, self.targets)
             self._barrier()
+        if check:
+            status = ops.device_status(self.device.index)
+            if status != 0:
+                raise PeerTimeoutError(self.rank, status)
         return mine
+
+
+class PeerTimeoutError(RuntimeError):
+    """A device-side wait of the fused d_ff split gave up (status word code ``code``,
+    6 = a peer barrier whose peer did not signal in time); the layer outputs of that
+    call are not valid.  The status word stays set until ``ops.clear_device_status``."""
+
+    def __init__(self, rank: int, code: int):
+        super().__init__(f"rank {rank}: fused d_ff split gave up waiting on the device (status {code}); "
+                         "its output is not valid")
+        self.rank = rank
+        self.code = code

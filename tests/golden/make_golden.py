@@ -1,9 +1,9 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference's own code.
 
-Run in a checkout where the reference is importable (the default path is the
-read-only reference tree of the build machine; pass another with --reference):
+Run with a checkout of the reference (thiagocmattar/sparsity-spillover), given by
+--reference or by the SPARSITY_SPILLOVER_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
 
 Every fixture is produced by executing the reference's modules, never the oracle:
 
@@ -23,6 +23,7 @@ Every fixture is produced by executing the reference's modules, never the oracle
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import sys
 from pathlib import Path
@@ -237,9 +238,12 @@ def measurement(ref: Path) -> dict:
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SPARSITY_SPILLOVER_REFERENCE"),
+                    help="path of a reference checkout (default: $SPARSITY_SPILLOVER_REFERENCE)")
     ap.add_argument("--only", nargs="*", help="fixture names to regenerate (default: all)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set SPARSITY_SPILLOVER_REFERENCE")
     ref = Path(args.reference)
     sys.path.insert(0, str(ref / "src"))
     torch.set_num_threads(1)

@@ -229,6 +229,89 @@ def test_corner_gate_respects_sequences():
     np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), obit.tile_bits(h_c))
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("b,s,d,f", [(7, 37, 128, 256), (5, 301, 256, 512), (3, 1000, 128, 1024)])
+def test_corner_gate_partial_final_blocks(dtype, b, s, d, f):
+    """Sequences whose length is not a multiple of 8 end with a shorter token block
+    decided by its own first row (tile_gate.py:25-28): h equals the reference gate of
+    the kernel's z with blocks restarting per sequence, the bitmap matches, and the
+    down projection of that h matches the oracle."""
+    from sparsity_spillover_b200 import ops
+
+    t = b * s
+    x, w_in, b_in, w_out, b_out = _inputs(t, d, f, dtype, seed=t + f)
+    kappa = _kappa(x, w_in, b_in, 0.3, dtype)
+    xd, wd, bd, wod, bod = _cuda(x, w_in, b_in, w_out, b_out)
+    z = torch.empty(t, f, dtype=dtype, device=DEV)
+    h, bits = ops.up_gate(xd, wd, bd, {"operator": "tile_corner_threshold", "kappa": kappa}, z_out=z, seq_len=s)
+    y = ops.down_sparse(h, bits, wod, bod, skip="fine")
+    torch.cuda.synchronize()
+    z_c, h_c = z.cpu(), h.cpu()
+    ref = og.corner(z_c.reshape(b, s, f), og.round_kappa(kappa, dtype)).reshape(t, f)
+    assert torch.equal(h_c, ref)
+    assert int((h_c != 0).sum()) > 0 and int((h_c == 0).sum()) > 0
+    np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), obit.tile_bits(h_c))
+    y_ref = omlp.down_from_h(h_c, w_out, b_out)
+    assert omlp.max_rel_error(y.cpu(), y_ref) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("skip", [True, "fine"])
+def test_cfg3_shape_up_gate_and_down_sparse(dtype, skip):
+    """The Pythia-410M layer shape (d=1024, F=4096) at 10 % element density on 2048
+    tokens: h bit-exact against the gate of the kernel's z, the bitmap exact, z and y
+    within tolerance of the fp32 oracle, and the skip counters equal to the oracle's."""
+    from sparsity_spillover_b200 import ops
+
+    t, d, f = 2048, 1024, 4096
+    x, w_in, b_in, w_out, b_out = _inputs(t, d, f, dtype, seed=410)
+    kappa = _kappa(x, w_in, b_in, 0.1, dtype)
+    spec = _spec(og.ONE_SIDED, kappa)
+    xd, wd, bd, wod, bod = _cuda(x, w_in, b_in, w_out, b_out)
+    r = torch.randn(t, d, generator=torch.Generator().manual_seed(411)).to(dtype)
+    z = torch.empty(t, f, dtype=dtype, device=DEV)
+    h, bits = ops.up_gate(xd, wd, bd, spec, z_out=z)
+    stats = torch.zeros(2, dtype=torch.int64, device=DEV)
+    y = ops.down_sparse(h, bits, wod, bod, r.to(DEV), skip=skip, stats=stats)
+    torch.cuda.synchronize()
+    z_c, h_c = z.cpu(), h.cpu()
+    assert omlp.max_rel_error(z_c, omlp.linear(x, w_in, b_in)) <= TOL[dtype]
+    assert torch.equal(h_c, og.apply(z_c, og.ONE_SIDED, spec.kappa_for(dtype)))
+    np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), obit.tile_bits(h_c))
+    y_ref = omlp.down_from_h(h_c, w_out, b_out, residual=r)
+    assert omlp.max_rel_error(y.cpu(), y_ref) <= TOL[dtype]
+    issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=d // 256, m_tile=ops.down_tile_tokens(skip))
+    assert stats.cpu().tolist() == [issued, skipped]
+
+
+@pytest.mark.parametrize("skip", [True, "fine"])
+def test_cfg2_full_size_tile_structured(skip):
+    """cfg2 at its full size (T=65536, d=512, F=2048, bf16, 64x64 tiles live with p=0.1):
+    the skipping down projection is bit-identical to its dense mode, its counters equal
+    the oracle's tile accounting over all tokens, and two token ranges (the first and
+    the last 2048 tokens) match the fp32 oracle."""
+    from sparsity_spillover_b200 import ops, workloads
+
+    t, d, f = 65536, 512, 2048
+    h, _ = workloads.tile_structured_h(t, f, 0.1, seed=612, device=DEV, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(613)
+    w_out = (torch.randn(d, f, generator=g) * 0.02).to(torch.bfloat16)
+    b_out = (torch.randn(d, generator=g) * 0.02).to(torch.bfloat16)
+    bits = ops.tile_bits_from_h(h)
+    stats = torch.zeros(2, dtype=torch.int64, device=DEV)
+    y = ops.down_sparse(h, bits, w_out.to(DEV), b_out.to(DEV), skip=skip, stats=stats)
+    y_dense = ops.down_sparse(h, None, w_out.to(DEV), b_out.to(DEV), skip=False)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_dense)
+    h_c = h.cpu()
+    issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=d // 256, m_tile=ops.down_tile_tokens(skip))
+    assert stats.cpu().tolist() == [issued, skipped]
+    assert skipped > 0
+    for rows in (slice(0, 2048), slice(t - 2048, t)):
+        y_ref = omlp.down_from_h(h_c[rows], w_out, b_out, dtype=torch.bfloat16)
+        assert omlp.max_rel_error(y.cpu()[rows], y_ref) <= TOL[torch.bfloat16]
+
+
 def test_invalid_arguments_raise():
     from sparsity_spillover_b200 import ops
     from sparsity_spillover_b200._lib import SpmlpError

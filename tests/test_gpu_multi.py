@@ -67,7 +67,7 @@ def _worker(rank, world, port, queue):
         status = ops.device_status(rank)
         # Failure detection without a fault: rank 0 waits for an epoch that rank 1 never
         # signals; the bounded wait gives up, the status word says so, the GPU keeps working.
-        timeout_status, usable = 6, True
+        timeout_status, usable, raised = 6, True, True
         if rank == 0:
             ops.clear_device_status(rank)
             ops.peer_barrier(fused.flag_slots, fused.flags, fused.epoch + 1000)
@@ -77,7 +77,15 @@ def _worker(rank, world, port, queue):
             probe = torch.zeros(64, 128, dtype=torch.float16, device=dev)
             probe[5, 70] = 1.0
             usable = ops.tile_bits_from_h(probe).cpu().tolist() == [2, 0, 0, 0]
-        queue.put((rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable))
+            # A whole forward while rank 1 stays out: its barriers give up, and forward
+            # reports it instead of returning the incomplete result.
+            try:
+                fused.forward(x)
+                raised = False
+            except sdist.PeerTimeoutError as exc:
+                raised = exc.code == 6
+            ops.clear_device_status(rank)
+        queue.put((rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable and raised))
     finally:
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()

@@ -10,6 +10,11 @@ the north-star tolerance (max|err| / max|ref| <= 2e-3 for fp16, 1e-2 for bf16).
 The second call uses fewer tokens and different inputs, so stale workspace
 contents from the first call (h or bitmap bits) would show up as errors.
 
+They also check it against the CPU oracle (fp32 GEMMs, the reference gate on
+the dtype-rounded z), and at the largest token count the static buffer holds
+for F = 2048 (8191 tokens: 2*T*F bytes of h plus the bitmap within 32 MiB),
+with one token more rejected.
+
 This file sorts last so that a run stopping at its first failure has already
 run every other test; it also passes on its own in a fresh process.
 """
@@ -83,6 +88,37 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(lib, dtype):
         torch.cuda.synchronize()
         assert _max_rel(y, y_ref) <= TOL[dtype]
         assert torch.equal(y, y_ref)  # same kernels, same inputs: deterministic
+
+
+def _oracle(args, kappa, dtype):
+    """fp32 oracle of the same forward: z = x w_in^T + b_in rounded to dtype, the
+    one-sided gate (kappa already a dtype value), y = h w_out^T + b_out + r in fp32."""
+    from oracle import gates as og
+    from oracle import mlp as omlp
+
+    x, w_in, b_in, w_out, b_out, r = (a.cpu() for a in args)
+    z = omlp.linear(x, w_in, b_in).to(dtype)
+    h = og.apply(z, og.ONE_SIDED, kappa)
+    return omlp.down_from_h(h, w_out, b_out, residual=r)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_noalloc_matches_the_oracle_up_to_the_buffer_limit(lib, dtype):
+    torch.cuda.init()
+    kappa = float(torch.tensor(0.58, dtype=dtype))
+    for t in (8191, 513):  # 8191 tokens fill the 32 MiB buffer at F = 2048; then a smaller call
+        args = _layer(t, 512, 2048, dtype, seed=t)
+        y = _noalloc(lib, args, kappa, dtype)
+        torch.cuda.synchronize()
+        assert _max_rel(y.cpu(), _oracle(args, kappa, dtype)) <= TOL[dtype]
+    args = _layer(8192, 512, 2048, dtype, seed=5)
+    x, w_in, b_in, w_out, b_out, r = args
+    y = torch.empty(8192, 512, dtype=dtype, device="cuda")
+    rc = lib.spmlp_mlp_forward_noalloc(x.data_ptr(), w_in.data_ptr(), b_in.data_ptr(), w_out.data_ptr(),
+                                       b_out.data_ptr(), r.data_ptr(), y.data_ptr(), 8192, 512, 2048, CODES[dtype],
+                                       ONE_SIDED, ctypes.c_float(kappa), 8192, DOWN_SKIP, None,
+                                       torch.cuda.current_stream().cuda_stream)
+    assert rc == -2  # one token past the limit: SPMLP_ESHAPE, nothing launched
 
 
 def test_noalloc_rejects_sizes_beyond_the_static_buffer(lib):
