@@ -11,7 +11,7 @@ The second call uses fewer tokens and different inputs, so stale workspace
 contents from the first call (h or bitmap bits) would show up as errors.
 
 They also check it against the CPU oracle (fp32 GEMMs, the reference gate on
-the dtype-rounded z), and at the largest token count the static buffer holds
+the kernel's dtype-rounded z), and at the largest token count the static buffer holds
 for F = 2048 (8191 tokens: 2*T*F bytes of h plus the bitmap within 32 MiB),
 with one token more rejected.
 
@@ -90,16 +90,30 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(lib, dtype):
         assert torch.equal(y, y_ref)  # same kernels, same inputs: deterministic
 
 
-def _oracle(args, kappa, dtype):
-    """fp32 oracle of the same forward: z = x w_in^T + b_in rounded to dtype, the
-    one-sided gate (kappa already a dtype value), y = h w_out^T + b_out + r in fp32."""
+def _oracle(lib, args, kappa, dtype):
+    """fp32 oracle of the same forward, on the kernel's own rounded z (the parity
+    convention of this library's tests: a z one ulp away from the oracle's can flip a
+    gate decision at kappa, so the gate is applied to the z the up projection
+    computed): h = one-sided gate of z, y = h w_out^T + b_out + r in fp32.  z comes
+    from spmlp_up_gate's z_out through the C ABI."""
     from oracle import gates as og
     from oracle import mlp as omlp
 
-    x, w_in, b_in, w_out, b_out, r = (a.cpu() for a in args)
-    z = omlp.linear(x, w_in, b_in).to(dtype)
-    h = og.apply(z, og.ONE_SIDED, kappa)
-    return omlp.down_from_h(h, w_out, b_out, residual=r)
+    x, w_in, b_in, w_out, b_out, r = args
+    t, d = x.shape
+    f = w_in.shape[0]
+    h = torch.empty(t, f, dtype=dtype, device="cuda")
+    z = torch.empty(t, f, dtype=dtype, device="cuda")
+    bits = torch.empty(int(lib.spmlp_tile_bits_size(t, f)), dtype=torch.int32, device="cuda")
+    rc = lib.spmlp_up_gate(x.data_ptr(), w_in.data_ptr(), b_in.data_ptr(), h.data_ptr(), bits.data_ptr(),
+                           z.data_ptr(), t, d, f, CODES[dtype], ONE_SIDED, ctypes.c_float(kappa), t,
+                           torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.spmlp_last_error()
+    torch.cuda.synchronize()
+    z_c = z.cpu()
+    assert _max_rel(z_c, omlp.linear(x.cpu(), w_in.cpu(), b_in.cpu())) <= TOL[dtype]
+    h_ref = og.apply(z_c, og.ONE_SIDED, kappa)
+    return omlp.down_from_h(h_ref, w_out.cpu(), b_out.cpu(), residual=r.cpu())
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -110,7 +124,7 @@ def test_noalloc_matches_the_oracle_up_to_the_buffer_limit(lib, dtype):
         args = _layer(t, 512, 2048, dtype, seed=t)
         y = _noalloc(lib, args, kappa, dtype)
         torch.cuda.synchronize()
-        assert _max_rel(y.cpu(), _oracle(args, kappa, dtype)) <= TOL[dtype]
+        assert _max_rel(y.cpu(), _oracle(lib, args, kappa, dtype)) <= TOL[dtype]
     args = _layer(8192, 512, 2048, dtype, seed=5)
     x, w_in, b_in, w_out, b_out, r = args
     y = torch.empty(8192, 512, dtype=dtype, device="cuda")
