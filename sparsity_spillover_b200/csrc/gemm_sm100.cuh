@@ -504,6 +504,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_r,
                       const __grid_constant__ CUtensorMap tm_a2, const __grid_constant__ CUtensorMap tm_b2,
+                      const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_b2h,
                       const GemmParams p) {
   using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
   constexpr int kGroups = Tr::kTileM / kBitsRows;  // 16-row bitmap groups per tile
@@ -588,8 +589,9 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
           b_row2 = c1;
         }
       }
-      // A half-width item loads half of B through the second B map (a box of BN/2/CG rows).
-      const CUtensorMap* map_b = half ? &tm_b2 : &tm_b;
+      // A half-width item loads half of B (and of the joint's B2) through maps with a
+      // box of BN/2/CG rows.
+      const CUtensorMap* map_b = half ? &tm_bh : &tm_b;
       const uint32_t stage_bytes = half ? Tr::kABytes + Tr::kBBytes / 2 : Tr::kStageBytes;
       // Load K-block kb of (ma, mb) into the next ring stage (warp-collective).
       auto issue = [&](const CUtensorMap* ma, const CUtensorMap* mb, int kb) -> bool {
@@ -627,7 +629,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
       };
       if constexpr (KIND == KIND_JOINT) {
         // The attention-output branch first: every K-block of z and Wo.
-        for (int kb = 0; kb < p.K2 / kBK && ok; ++kb) ok = issue(&tm_a2, &tm_b2, kb);
+        for (int kb = 0; kb < p.K2 / kBK && ok; ++kb) ok = issue(&tm_a2, half ? &tm_b2h : &tm_b2, kb);
         if (!ok) break;
       }
       if constexpr ((KIND == KIND_DOWN || KIND == KIND_JOINT) && CG == 1) {

@@ -186,7 +186,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr,
-                const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr) {
+                const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr,
+                const CUtensorMap* tbh = nullptr, const CUtensorMap* tb2h = nullptr) {
   using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
   auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING, LN>;
   // Setting the attribute is per function; cheap and idempotent.
@@ -237,9 +238,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     units = max_clusters[dev_id];
   }
   // The last round of the persistent grid: when it would leave at least half of the
-  // units idle, its tiles run as two half-width items each (down projection with
-  // four epilogue warps, each of which owns all columns of its rows).
-  if constexpr (KIND == KIND_DOWN && EPI == 4 && RING > 0) {
+  // units idle, its tiles run as two half-width items each (the down projection and
+  // the joint consumer, whose epilogue warps write through an output ring).
+  if constexpr ((KIND == KIND_DOWN || KIND == KIND_JOINT) && RING > 0) {
     if (p.split_tail && tiles > units) {
       const int rem = tiles % units;
       if (rem > 0 && 2 * rem <= units) {
@@ -251,7 +252,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   if (p.work_items < units) units = p.work_items;
   cfg.gridDim = dim3(units * CG);
   e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr != nullptr ? *tr : tc, ta2 != nullptr ? *ta2 : ta,
-                         tb2 != nullptr ? *tb2 : tb, p);
+                         tb2 != nullptr ? *tb2 : tb, tbh != nullptr ? *tbh : tb, tb2h != nullptr ? *tb2h : tb, p);
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
@@ -462,11 +463,11 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps, RF = kDownFineRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
   if (fine) {
-    if (bf16) return launch_gemm<KIND_DOWN, 0, BNF, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
-    return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BNF, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+    return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
   }
-  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
-  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb_half);
+  if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+  return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
 }
 
 int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w2, const void* b2, const void* wo,
@@ -488,11 +489,14 @@ int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w
   const bool bf16 = dtype == SPMLP_BF16;
   constexpr int BN = kJointBN;
   const int cg = mode == SPMLP_DOWN_SKIP_FINE ? 1 : 2;
-  CUtensorMap ta, tb, ta2, tb2, tc, tr;
+  CUtensorMap ta, tb, ta2, tb2, tc, tr, tb_half, tb2_half;
   if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
   if ((rc = make_kmajor_map(&tb, w2, d, F, BN / cg, bf16))) return rc;
   if ((rc = make_kmajor_map(&ta2, z, T, d, kBM, bf16))) return rc;
   if ((rc = make_kmajor_map(&tb2, wo, d, d, BN / cg, bf16))) return rc;
+  // half-width tail items (the last round of the persistent grid) load half of each B
+  if ((rc = make_kmajor_map(&tb_half, w2, d, F, BN / 2 / cg, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb2_half, wo, d, d, BN / 2 / cg, bf16))) return rc;
   if ((rc = make_out_map(&tc, out, T, d, bf16))) return rc;
   if (residual != nullptr && (rc = make_out_map(&tr, residual, T, d, bf16))) return rc;
   GemmParams p{};
@@ -509,16 +513,17 @@ int joint_impl(const void* h, const uint32_t* bits, const void* z, const void* w
   p.bits_words = spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
+  p.split_tail = 1;
   constexpr int R = kJointRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
   if (mode == SPMLP_DOWN_SKIP_FINE) {
     constexpr int S = kJointFineStages, E = kJointFineEpiWarps;
-    if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
-    return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+    if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2, &tb_half, &tb2_half);
+    return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 1, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2, &tb_half, &tb2_half);
   }
   constexpr int S = kJointStages, E = kJointEpiWarps;
-  if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
-  return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2);
+  if (bf16) return launch_gemm<KIND_JOINT, 0, BN, S, true, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2, &tb_half, &tb2_half);
+  return launch_gemm<KIND_JOINT, 0, BN, S, false, E, 2, R>(ta, tb, tc, p, stream, dev, trp, &ta2, &tb2, &tb_half, &tb2_half);
 }
 
 // A bounded wait on an mbarrier that nothing arrives on: the same wait helper every
@@ -748,8 +753,8 @@ int head_impl(const void* x, const uint32_t* support, const void* w, void* logit
   }
   if (pairs) {
     constexpr int SP = kHeadPairStages, EP = kHeadPairEpiWarps, RP = kHeadPairRing;
-    if (bf16) return launch_gemm<KIND_HEAD, 0, 2 * BN, SP, true, EP, 2, RP>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb_half);
-    return launch_gemm<KIND_HEAD, 0, 2 * BN, SP, false, EP, 2, RP>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb_half);
+    if (bf16) return launch_gemm<KIND_HEAD, 0, 2 * BN, SP, true, EP, 2, RP>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb, &tb_half);
+    return launch_gemm<KIND_HEAD, 0, 2 * BN, SP, false, EP, 2, RP>(ta, tb, tc, p, stream, dev, nullptr, &ta, &tb, &tb_half);
   }
   constexpr int S = kHeadStages, E = kHeadEpiWarps, R = kHeadRing;
   if (bf16) return launch_gemm<KIND_HEAD, 0, BN, S, true, E, 1, R>(ta, tb, tc, p, stream, dev);

@@ -133,6 +133,39 @@ def test_joint_skips_dead_tiles_of_h_and_counts_them(skip):
     assert skipped > 0
 
 
+@pytest.mark.parametrize("skip", [True, "fine"])
+def test_joint_last_round_split_items_match_the_oracle(skip):
+    """At T=32768, d=512 the joint's persistent grid runs its last round of tiles as
+    half-width items (both products, both column halves): the final token blocks match
+    the oracle, and the issued / skipped counters equal the oracle's accounting over
+    all tokens (tile-structured h, so whole K-blocks are skipped)."""
+    from sparsity_spillover_b200 import ops, workloads
+
+    dtype, t, d, f = torch.bfloat16, 32768, 512, 2048
+    h, _ = workloads.tile_structured_h(t, f, 0.3, seed=21, device="cuda", dtype=dtype)
+    g = torch.Generator().manual_seed(22)
+    z = torch.randn(t, d, generator=g).to(dtype)
+    w2 = (torch.randn(d, f, generator=g) * 0.02).to(dtype)
+    b2 = (torch.randn(d, generator=g) * 0.02).to(dtype)
+    wo = (torch.randn(d, d, generator=g) * 0.02).to(dtype)
+    bo = (torch.randn(d, generator=g) * 0.02).to(dtype)
+    r = torch.randn(t, d, generator=g).to(dtype)
+    bits = ops.tile_bits_from_h(h)
+    stats = torch.zeros(2, dtype=torch.int64, device="cuda")
+    out = ops.joint(h, bits, z.cuda(), w2.cuda(), b2.cuda(), wo.cuda(), bo.cuda(), r.cuda(), skip=skip, stats=stats)
+    torch.cuda.synchronize()
+    h_c = h.cpu()
+    tail = slice(t - 4096, t)
+    ref = omlp.joint(h_c[tail], z[tail], w2, b2, wo, bo, r[tail], 0.0, 0.0, False, False)
+    assert omlp.max_rel_error(out.cpu()[tail], ref) <= TOL[dtype]
+    head = slice(0, 1024)
+    ref0 = omlp.joint(h_c[head], z[head], w2, b2, wo, bo, r[head], 0.0, 0.0, False, False)
+    assert omlp.max_rel_error(out.cpu()[head], ref0) <= TOL[dtype]
+    issued, skipped = obit.skip_counts(obit.tile_mask(h_c.float(), 16, 64), f, n_tiles=d // 256,
+                                       m_tile=ops.down_tile_tokens(skip))
+    assert stats.cpu().tolist() == [issued, skipped]
+
+
 class FixedOneSidedThreshold(torch.nn.Module):  # the reference gate module's name, attribute and rule
     def __init__(self, kappa):
         super().__init__()
