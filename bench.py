@@ -320,6 +320,49 @@ def tile_structured(device, steps=10) -> list[dict]:
     return rows
 
 
+def corner_tiles_cfg1(device, steps=10) -> list[dict]:
+    """The down projection on h with the reference's corner-tile structure (8-token x
+    16-feature tiles kept whole with probability p; cfg1 layer shape T=32768, d=512,
+    F=2048, fp16): every mode, with the skipped K16 fraction against the ideal (the
+    dead 16x16 granules), and cuBLAS."""
+    import torch
+
+    from sparsity_spillover_b200 import ops, workloads
+
+    t, d, f = 32768, 512, 2048
+    g = torch.Generator(device=device).manual_seed(61)
+    w = (torch.randn(d, f, generator=g, device=device) * 0.02).half()
+    y = torch.empty(t, d, dtype=torch.float16, device=device)
+    rows = []
+    for p in (0.01, 0.02, 0.05):
+        h, kept = workloads.corner_tile_h(t, f, p, seed=int(p * 1000) + 3, device=device)
+        b64, b16 = ops.tile_bits_from_h(h), ops.tile_bits16_from_h(h)
+        import numpy as np
+
+        live16 = float(np.unpackbits(b16.cpu().numpy().view(np.uint8)).mean())  # F/16 = 128: every bit is a tile
+        density = float((h != 0).float().mean())
+        # ideal: the skipped fraction if every dead 16x16 tile (the finest granule a 16-row
+        # MMA could skip) were skipped, and the element-level zero fraction
+        row = {"p": p, "kept_tile_fraction": round(kept, 4), "element_density": round(density, 4),
+               "ideal_skipped_fraction_16x16": 1.0 - live16, "ideal_skipped_fraction_elements": 1.0 - density}
+        for mode in (False, True, "fine", "compact", "compact_fine"):
+            bits = b16 if isinstance(mode, str) and mode.startswith("compact") else b64
+            st = torch.zeros(2, dtype=torch.int64, device=device)
+            ops.down_sparse(h, bits, w, None, skip=mode, y=y, stats=st)
+            issued, skipped = st.tolist()
+            name = {False: "dense", True: "coarse"}.get(mode, mode)
+            row[f"{name}_us"] = time_device(lambda: ops.down_sparse(h, bits, w, None, skip=mode, y=y), steps,
+                                            device) * 1e6
+            row[f"{name}_skipped_k16_fraction"] = skipped / max(1, issued + skipped)
+        row["cublas_us"] = time_device(lambda: torch.nn.functional.linear(h, w), steps, device) * 1e6
+        best = min(("fine", "compact_fine", "coarse", "dense", "compact"), key=lambda m: row[f"{m}_us"])
+        row["best_mode"] = best
+        row["best_speedup_vs_cublas"] = row["cublas_us"] / row[f"{best}_us"]
+        rows.append(row)
+        del h, b64, b16
+    return rows
+
+
 def cfg3_410m(device, steps=3) -> dict:
     """cfg3: Pythia-410M shape, 24 layers, d=1024 F=4096, T=32768 per GPU, fp16, 10% density."""
     import torch
@@ -703,6 +746,12 @@ def summarize(line: dict) -> dict:
                                                    r(x["cublas_us"], 1), r(x["skipped_k16_fraction_fine"])]
                           for x in c2}
         out["cfg2_us_fields"] = ["fine", "coarse", "cublas", "skipped_k16_fraction_fine"]
+    ct = line.get("corner_tiles_cfg1")
+    if isinstance(ct, list):
+        out["corner_tiles_us"] = {f"p{x['p']}": [r(x["dense_us"], 1), r(x["fine_us"], 1), r(x["compact_fine_us"], 1),
+                                                 r(x["cublas_us"], 1), r(x["compact_fine_skipped_k16_fraction"])]
+                                  for x in ct}
+        out["corner_tiles_us_fields"] = ["dense", "fine", "compact_fine", "cublas", "skipped_k16_fraction_compact_fine"]
     c3 = line.get("pythia410m_cfg3")
     if isinstance(c3, dict) and "tokens_per_s" in c3:
         out["cfg3_mtok_s"] = r(c3["tokens_per_s"] / 1e6)
@@ -969,6 +1018,7 @@ def run_ours(args):
             line["joint_cfg1"] = _extra(joint_cfg1, device)
             line["layernorm_fold_cfg1"] = _extra(layernorm_fold_cfg1, device)
             line["cfg0_block"] = _extra(cfg0_block, device)
+            line["corner_tiles_cfg1"] = _extra(corner_tiles_cfg1, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, DENSITY)
     if world > 1:

@@ -61,6 +61,15 @@ extern "C" {
 #define SPMLP_DOWN_SKIP_FINE 2 /* as SPMLP_DOWN_SKIP with 128-token tiles on single
                               CTAs: skips more K-blocks when zeros come in token
                               blocks narrower than 256 (e.g. 64-token tiles)        */
+#define SPMLP_DOWN_COMPACT 3 /* compact mode (the survey's "mode 2 compact"): the bitmap
+                              is the 16x16 one (spmlp_tile_bits16_from_h); each
+                              pipeline stage gathers four live 16-feature granules of
+                              the tile (the union over its tokens) into shared memory,
+                              and only those are loaded and multiplied; 256-token tiles
+                              on CTA pairs.  For zeros structured at 16 features, e.g.
+                              the reference's 8x16 corner-tile gate
+                              (runs/063-2026-10-07-pythia14m-tile-specialized-kernel/tile_gate.py:9-33) */
+#define SPMLP_DOWN_COMPACT_FINE 4 /* SPMLP_DOWN_COMPACT with 128-token tiles on single CTAs */
 
 /* error codes (negative returns) */
 #define SPMLP_EINVAL -1   /* bad argument (null pointer, bad enum, non-finite kappa) */
@@ -96,6 +105,16 @@ int64_t spmlp_mask_encoded_size(const uint32_t* tile_bits, int64_t T, int F, int
 int64_t spmlp_mask_encode(const uint32_t* tile_bits, int64_t T, int F, int encoding, void* out, int64_t capacity);
 int spmlp_mask_decode_header(const void* data, int64_t n, int64_t* T, int* F, int* encoding);
 int spmlp_mask_decode(const void* data, int64_t n, uint32_t* tile_bits, int64_t capacity_words);
+
+/* 16x16 tile bitmap of an existing h [T,F] for the compact down modes: bit g % 32 of
+ * word r * spmlp_tile_bits16_words(F) + g / 32 is set iff tile (16-row group r,
+ * 16-feature group g) holds a nonzero (-0.0 counts as zero); every word is written.
+ * spmlp_tile_bits16_size gives the words for T tokens.  No reference counterpart:
+ * the reference derives its K16 masks inside the consumer
+ * (runs/042-2026-09-20-pythia70m-sparse-scale/kernel/joint/joint.cu:14-31). */
+int spmlp_tile_bits16_words(int F);
+int64_t spmlp_tile_bits16_size(int64_t T, int F);
+int spmlp_tile_bits16_from_h(const void* h, uint32_t* tile_bits16, int64_t T, int F, void* stream);
 
 /* Tile bitmap of an existing h [T,F] (same bit semantics as spmlp_up_gate's;
  * for callers whose h does not come from spmlp_up_gate).  Overwrites every
@@ -146,7 +165,9 @@ int spmlp_up_gate_ln(const void* x, const void* w_fold, const float* ln_s, const
  *   w_out [d,F], b_out [d] (nullable), residual [T,d] (nullable) -> y [T,d]
  *   y = round(h w_out^T + b_out), then round(y + residual) when given.
  *   A K-block (64 features) is skipped for a tile of spmlp_down_tile_tokens(mode)
- *   tokens when every 16x64 bitmap tile of it in that token range is zero.
+ *   tokens when every 16x64 bitmap tile of it in that token range is zero; in the
+ *   compact modes tile_bits is the 16x16 bitmap and a 16-feature granule is skipped
+ *   when every 16x16 tile of it in that token range is zero.
  *   stats (nullable, 2 x uint64, accumulated): [0] issued K16 MMA steps,
  *   [1] skipped K16 MMA steps; one step is one tcgen05.mma over a
  *   spmlp_down_tile_tokens(mode) x 256 output tile.

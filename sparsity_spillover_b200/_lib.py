@@ -27,6 +27,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_mask_decode_header": (I32, [VP, I64, _c.POINTER(I64), _c.POINTER(I32), _c.POINTER(I32)]),
     "spmlp_mask_decode": (I32, [VP, I64, VP, I64]),
     "spmlp_tile_bits_from_h": (I32, [VP, VP, I64, I32, I32, VP]),
+    "spmlp_tile_bits16_words": (I32, [I32]),
+    "spmlp_tile_bits16_size": (I64, [I64, I32]),
+    "spmlp_tile_bits16_from_h": (I32, [VP, VP, I64, I32, VP]),
     "spmlp_up_gate": (I32, [VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
     "spmlp_row_stats": (I32, [VP, VP, VP, I64, I32, I32, F32, VP]),
     "spmlp_up_gate_ln": (I32, [VP, VP, VP, VP, VP, VP, VP, VP, VP, I64, I32, I32, I32, I32, F32, I64, VP]),
@@ -51,7 +54,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 # Constants of include/spmlp.h.
 F16, BF16 = 0, 1
 GATE_IDENTITY, GATE_GELU, GATE_ONE_SIDED, GATE_SYMMETRIC, GATE_RELU, GATE_GELU_MASKED, GATE_CORNER = range(7)
-DOWN_DENSE, DOWN_SKIP, DOWN_SKIP_FINE = 0, 1, 2
+DOWN_DENSE, DOWN_SKIP, DOWN_SKIP_FINE, DOWN_COMPACT, DOWN_COMPACT_FINE = 0, 1, 2, 3, 4
 MASK_RAW, MASK_ROW_RUNS = 0, 1
 HEAD_GATE_NONE, HEAD_GATE_K, HEAD_GATE_N = 0, 1, 2
 

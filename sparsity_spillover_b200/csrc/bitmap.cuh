@@ -165,4 +165,38 @@ __global__ void __launch_bounds__(256) corner_gate_kernel(uint16_t* z, uint32_t*
   for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
 }
 
+// The 16x16 tile bitmap of h (the compact down mode's): one bit per 16-row x 16-feature
+// tile, bit g % 32 of word r * words + g / 32 set iff the tile holds a nonzero (-0.0
+// counts as zero).  One CTA per 16-row group; each warp scans two tiles per pass: lane l
+// reads the 16-byte half (l & 1) of row (l >> 1) & 15 of tile 2 pass + l / 32 ... as two
+// 16-lane halves, one tile each.
+__global__ void __launch_bounds__(256) tile_bits16_kernel(const uint16_t* __restrict__ h, uint32_t* __restrict__ bits,
+                                                          int T, int F, int words) {
+  extern __shared__ uint32_t s_words[];
+  const int rg = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) s_words[w] = 0u;
+  __syncthreads();
+  const int tiles = F / 16;
+  const int half = lane >> 4;            // which of the pass's two tiles
+  const int row = rg * 16 + (lane & 15);  // one row of the tile per lane (32 bytes)
+  for (int g0 = 2 * warp; g0 < tiles; g0 += 2 * nwarps) {
+    const int g = g0 + half;
+    uint32_t acc = 0;
+    if (row < T && g < tiles) {
+      const uint4* p = reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * F + g * 16);
+      const uint4 a = __ldcs(p), b = __ldcs(p + 1);
+      acc = (a.x | a.y | a.z | a.w | b.x | b.y | b.z | b.w) & 0x7fff7fffu;
+    }
+    const uint32_t ball = __ballot_sync(0xffffffffu, acc != 0);
+    if (lane == 0) {
+      if (ball & 0x0000ffffu) atomicOr(&s_words[g0 >> 5], 1u << (g0 & 31));
+      if ((ball & 0xffff0000u) && g0 + 1 < tiles) atomicOr(&s_words[(g0 + 1) >> 5], 1u << ((g0 + 1) & 31));
+    }
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
+}
+
 }  // namespace spmlp

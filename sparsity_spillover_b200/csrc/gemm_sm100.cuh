@@ -294,14 +294,38 @@ __device__ __forceinline__ bool for_each_live_kblock_ahead(const GemmParams& p, 
   return true;
 }
 
+// Enumerate the live 16-feature granules of an M-tile of GROUPS 16-row groups in
+// increasing K (16x16 bitmap), calling f(g); without skipping every granule.
+// Warp-collective (all 32 lanes must call it with the same arguments).
+template <int GROUPS, class F>
+__device__ __forceinline__ bool for_each_live_g16(const GemmParams& p, int m_blk, int lane, F&& f) {
+  const int granules = p.K / 16;
+  if (!p.skip || p.bits_in == nullptr) {
+    for (int g = 0; g < granules; ++g)
+      if (!f(g)) return false;
+    return true;
+  }
+  const int row_groups = (p.M + kBitsRows - 1) / kBitsRows;
+  const int chunks = (granules + 31) / 32;
+  for (int c = 0; c < chunks; ++c) {
+    uint32_t pending = live_chunk<GROUPS>(p.bits_in, p.bits_words, row_groups, m_blk, c, granules, lane);
+    while (pending) {
+      const int g = c * 32 + __ffs(pending) - 1;
+      pending &= pending - 1;
+      if (!f(g)) return false;
+    }
+  }
+  return true;
+}
+
 // Whether an M-tile of GROUPS 16-row groups has any live K granule (warp-collective),
 // i.e. whether for_each_live_kblock would visit any K-block: one bitmap word per lane
 // (lane i reads word i of the tile's GROUPS x chunks words) instead of GROUPS per lane.
-template <int KIND, int GROUPS>
+template <int KIND, int GROUPS, bool G16 = false>
 __device__ __forceinline__ bool any_live(const GemmParams& p, int m_blk, int lane) {
   if (!p.skip || p.bits_in == nullptr) return p.K >= kBK;
   const int row_groups = (p.M + kBitsRows - 1) / kBitsRows;
-  const int granules = k_granules<KIND>(p.K);
+  const int granules = G16 ? p.K / 16 : k_granules<KIND>(p.K);
   const int chunks = (granules + 31) / 32;
   uint32_t any = 0;
   for (int i = lane; i < GROUPS * chunks; i += 32) {
@@ -499,7 +523,11 @@ struct JointEpilogue {
 // completion is counted on the leader's barriers; commits multicast to both.
 // LN (KIND_UP only): the epilogue applies a LayerNorm folded into the weight
 // (GemmParams::ln_*); a compile-time switch so the plain up projection carries none of it.
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false>
+// G16 (KIND_DOWN): the compact mode -- the skip bitmap has 16x16 granules and each stage
+// gathers four live 16-feature granules of K (A and B boxes of 16 columns, 32-byte
+// swizzle), one K16 MMA each, so only live granules are loaded and multiplied.
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false,
+          bool G16 = false>
 __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_r,
@@ -632,7 +660,52 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         for (int kb = 0; kb < p.K2 / kBK && ok; ++kb) ok = issue(&tm_a2, half ? &tm_b2h : &tm_b2, kb);
         if (!ok) break;
       }
-      if constexpr ((KIND == KIND_DOWN || KIND == KIND_JOINT) && CG == 1) {
+      if constexpr (G16) {
+        // Four live 16-feature granules per stage: slot j holds the granule's 128 rows of
+        // A (4 KiB) and BN/CG rows of B, each a 32B-swizzled box of 16 columns.
+        constexpr uint32_t kSlotA = kBM * 32, kSlotB = (BN / CG) * 32;
+        const uint32_t slot_bytes = kSlotA + (half ? kSlotB / 2 : kSlotB);
+        int j = 0;
+        auto flush = [&]() -> bool {  // the stage holds j granules: arm its barrier, move on
+          if (lane == 0) {
+            if constexpr (CG == 1)
+              mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(j) * slot_bytes);
+            else if (leader)
+              mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(CG * j) * slot_bytes);
+          }
+          __syncwarp();
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          j = 0;
+          return true;
+        };
+        ok = for_each_live_g16<kGroups>(p, m_blk, lane, [&](int g) -> bool {
+          bool good = true;
+          if (lane == 0) {
+            if (j == 0) good = mbar_wait(&empty[stage], phase ^ 1u, p.status, st0, kDevTimeoutProducer);
+            if (good) {
+              uint8_t* a_dst = s_a + stage * Tr::kABytes + j * kSlotA;
+              uint8_t* b_dst = s_b + stage * Tr::kBBytes + j * kSlotB;
+              if constexpr (CG == 1) {
+                tma_load_2d(a_dst, &tm_a, &full[stage], g * 16, a_row, 0ull);
+                tma_load_2d(b_dst, map_b, &full[stage], g * 16, b_row, pol_b);
+              } else {
+                const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                tma_load_2d_pair(a_dst, &tm_a, bar, g * 16, a_row, 0ull);
+                tma_load_2d_pair(b_dst, map_b, bar, g * 16, b_row, pol_b);
+              }
+            }
+          }
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (!good) return false;
+          if (++j == 4) flush();
+          return true;
+        });
+        if (ok && j > 0) flush();
+      } else if constexpr ((KIND == KIND_DOWN || KIND == KIND_JOINT) && CG == 1) {
         // A is h, mostly in HBM (written by the up projection, larger than L2): bring
         // its tiles into L2 kPrefetchAhead live K-blocks ahead of the loads.  This pays
         // for the single-CTA skipping kernels (4-6 % on tile-structured h); the pair
@@ -698,7 +771,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         // A tile without live K-blocks needs no MMA: the epilogue writes the
         // zero-accumulator result itself (the joint always has its z branch).  The live
         // K16 steps of the others are counted while their MMAs are issued below.
-        if (KIND != KIND_JOINT && !any_live<KIND, kGroups>(p, m_blk, lane)) {
+        if (KIND != KIND_JOINT && !any_live<KIND, kGroups, G16>(p, m_blk, lane)) {
           skipped_steps += weight * static_cast<unsigned long long>(k_steps_total);
           continue;
         }
@@ -743,10 +816,46 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         }
         uint32_t accumulate = 0;
         int live_steps = 0;
-        ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int, uint32_t k16) {
-          live_steps += __popc(k16);
-          return mma_stage(d_tmem, k16, accumulate);
-        });
+        if constexpr (G16) {
+          // One K16 MMA per gathered granule, four per stage (the producer's grouping).
+          constexpr uint32_t kSlotA = kBM * 32, kSlotB = (BN / CG) * 32;
+          int j = 0;
+          auto release_stage = [&]() {
+            if (lane == 0) umma_commit<CG>(&empty[stage]);
+            __syncwarp();
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            j = 0;
+          };
+          ok = for_each_live_g16<kGroups>(p, m_blk, lane, [&](int) -> bool {
+            bool good = true;
+            if (lane == 0) {
+              if (j == 0) {
+                good = mbar_wait(&full[stage], phase, p.status, st0, kDevTimeoutMma);
+                if (good) tc_fence_after();
+              }
+              if (good) {
+                const uint64_t a_desc = sw32_kmajor_desc(smem_u32(s_a + stage * Tr::kABytes + j * kSlotA));
+                const uint64_t b_desc = sw32_kmajor_desc(smem_u32(s_b + stage * Tr::kBBytes + j * kSlotB));
+                umma_f16<CG>(d_tmem, a_desc, b_desc, idesc, accumulate);
+                accumulate = 1;
+              }
+            }
+            good = __shfl_sync(0xffffffffu, good, 0);
+            if (!good) return false;
+            ++live_steps;
+            if (++j == 4) release_stage();
+            return true;
+          });
+          if (ok && j > 0) release_stage();
+        } else {
+          ok = for_each_live_kblock<KIND, kGroups>(p, m_blk, lane, [&](int, uint32_t k16) {
+            live_steps += __popc(k16);
+            return mma_stage(d_tmem, k16, accumulate);
+          });
+        }
         if (!ok) break;
         skipped_steps += weight * static_cast<unsigned long long>(k_steps_total - live_steps);
         issued_steps += weight * static_cast<unsigned long long>(live_steps);
@@ -858,7 +967,7 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         return n_col0 + ch * 32;
       };
       int live_blocks = 1;  // > 0: the MMA warp wrote this item's accumulator
-      if constexpr (KIND != KIND_UP) live_blocks = any_live<KIND, kGroups>(p, m_blk, lane) ? 1 : 0;
+      if constexpr (KIND != KIND_UP) live_blocks = any_live<KIND, kGroups, G16>(p, m_blk, lane) ? 1 : 0;
       const int row0 = m_blk * Tr::kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;

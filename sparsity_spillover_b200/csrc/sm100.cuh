@@ -352,6 +352,19 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
+// The same for a tile written with 32-byte swizzling: rows of 16 fp16/bf16 (32 B, one
+// K16 step), 8-row swizzle atoms of 256 B (stride byte offset 256 B), layout
+// SWIZZLE_32B = 6.
+__device__ __forceinline__ uint64_t sw32_kmajor_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(256u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(6u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16: fp32 accumulator, both operands K-major.
 // bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 = f16, 1 = bf16),
 // 17-22 N >> 3, 24-28 M >> 4.

@@ -150,17 +150,20 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// K-major operand [rows, k] -> box of 64 (k) x box_rows, 128-byte swizzle.
-int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, bool bf16) {
+// K-major operand [rows, k] -> box of 64 (k) x box_rows, 128-byte swizzle; with
+// box_k = 16, a box of one K16 step (32 bytes per row) and 32-byte swizzle.
+int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, bool bf16,
+                    int box_k = kBK) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(SPMLP_EDRIVER, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_k), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = box_k == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SPMLP_EDRIVER, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
   return 0;
 }
@@ -183,13 +186,14 @@ int make_out_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------- launch
-template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false>
+template <int KIND, int GATE, int BN, int STAGES, bool BF16, int EPI, int CG, int RING = 0, bool LN = false,
+          bool G16 = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, DeviceInfo* dev, const CUtensorMap* tr = nullptr,
                 const CUtensorMap* ta2 = nullptr, const CUtensorMap* tb2 = nullptr,
                 const CUtensorMap* tbh = nullptr, const CUtensorMap* tb2h = nullptr) {
   using Tr = GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RING>;
-  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING, LN>;
+  auto kernel = gemm_sm100_kernel<KIND, GATE, BN, STAGES, BF16, EPI, CG, RING, LN, G16>;
   // Setting the attribute is per function; cheap and idempotent.
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
@@ -418,8 +422,9 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
     y = slots[0];  // the output map is encoded but not stored through in this mode
   }
   if (!h || !w_out || !y) return fail(SPMLP_EINVAL, "h, w_out and y must be non-null");
-  if (mode != SPMLP_DOWN_DENSE && mode != SPMLP_DOWN_SKIP && mode != SPMLP_DOWN_SKIP_FINE)
-    return fail(SPMLP_EINVAL, "unknown down mode %d", mode);
+  if (mode < SPMLP_DOWN_DENSE || mode > SPMLP_DOWN_COMPACT_FINE) return fail(SPMLP_EINVAL, "unknown down mode %d", mode);
+  const bool compact = mode == SPMLP_DOWN_COMPACT || mode == SPMLP_DOWN_COMPACT_FINE;
+  if (compact && slots != nullptr) return fail(SPMLP_EINVAL, "the scattering down projection takes the 16x64 modes");
   if (mode != SPMLP_DOWN_DENSE && !bits) return fail(SPMLP_EINVAL, "the skipping down modes need tile_bits");
   if ((rc = check_dtype(dtype))) return rc;
   if ((rc = check_mk(T, F, d, "F", "d"))) return rc;
@@ -431,14 +436,15 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
   constexpr int BN = 256, BNF = kDownFineBN;
-  const bool fine = mode == SPMLP_DOWN_SKIP_FINE;
+  const bool fine = mode == SPMLP_DOWN_SKIP_FINE || mode == SPMLP_DOWN_COMPACT_FINE;
   const int bn = fine ? BNF : BN;
+  const int box_k = compact ? 16 : kBK;  // compact: gathered K16 granules, 32-byte swizzle
   CUtensorMap ta, tb;
-  if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16))) return rc;
+  if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16, box_k))) return rc;
   const int cg = fine ? 1 : kDownCG;
-  if ((rc = make_kmajor_map(&tb, w_out, d, F, bn / cg, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb, w_out, d, F, bn / cg, bf16, box_k))) return rc;
   CUtensorMap tb_half;  // half-width tail items load bn/2 columns of w_out
-  if ((rc = make_kmajor_map(&tb_half, w_out, d, F, bn / 2 / cg, bf16))) return rc;
+  if ((rc = make_kmajor_map(&tb_half, w_out, d, F, bn / 2 / cg, bf16, box_k))) return rc;
   CUtensorMap tc, tr;
   if ((rc = make_out_map(&tc, y, T, d, bf16))) return rc;
   if (residual != nullptr && (rc = make_out_map(&tr, residual, T, d, bf16))) return rc;
@@ -451,7 +457,7 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   p.out = y;
   p.residual = residual;
   p.bits_in = bits;
-  p.bits_words = spmlp_tile_bits_words(F);
+  p.bits_words = compact ? spmlp_tile_bits16_words(F) : spmlp_tile_bits_words(F);
   p.skip = mode == SPMLP_DOWN_DENSE ? 0 : 1;
   p.stats = reinterpret_cast<unsigned long long*>(stats);
   p.split_tail = 1;
@@ -462,6 +468,14 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   constexpr int S = kDownStages, E = kDownEpiWarps, C = kDownCG, R = kDownRing;
   constexpr int SF = kDownFineStages, EF = kDownFineEpiWarps, RF = kDownFineRing;
   const CUtensorMap* trp = residual != nullptr ? &tr : nullptr;
+  if (compact) {
+    if (fine) {
+      if (bf16) return launch_gemm<KIND_DOWN, 0, BNF, SF, true, EF, 1, RF, false, true>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+      return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF, false, true>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+    }
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R, false, true>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+    return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R, false, true>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+  }
   if (fine) {
     if (bf16) return launch_gemm<KIND_DOWN, 0, BNF, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
     return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
@@ -674,6 +688,23 @@ int tile_bits_impl(const void* h, uint32_t* bits, int64_t T, int F, int dtype, c
   return 0;
 }
 
+int tile_bits16_impl(const void* h, uint32_t* bits, int64_t T, int F, cudaStream_t stream) {
+  int rc;
+  if (!h || !bits) return fail(SPMLP_EINVAL, "h and tile_bits16 must be non-null");
+  if (T < 1 || T >= (int64_t(1) << 31)) return fail(SPMLP_ESHAPE, "T must be in [1, 2^31)");
+  if (F < kBitsCols || F % kBitsCols) return fail(SPMLP_ESHAPE, "F=%d must be a positive multiple of 64", F);
+  if (!aligned16(h)) return fail(SPMLP_EALIGN, "h must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  if ((rc = current_device_info(&dev))) return rc;
+  const int words = spmlp_tile_bits16_words(F);
+  const int groups = static_cast<int>((T + kBitsRows - 1) / kBitsRows);
+  tile_bits16_kernel<<<groups, 256, static_cast<size_t>(words) * 4, stream>>>(static_cast<const uint16_t*>(h), bits,
+                                                                              static_cast<int>(T), F, words);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tile_bits16_kernel launch");
+  return 0;
+}
+
 int head_prepare_impl(const float* x, void* x_out, uint32_t* support, int64_t T, int d, int dtype, float kappa,
                       cudaStream_t stream) {
   int rc;
@@ -857,7 +888,9 @@ extern "C" {
 
 int spmlp_version(void) { return 100; }
 
-int spmlp_down_tile_tokens(int mode) { return mode == SPMLP_DOWN_SKIP_FINE ? kBM : kBM * kDownCG; }
+int spmlp_down_tile_tokens(int mode) {
+  return (mode == SPMLP_DOWN_SKIP_FINE || mode == SPMLP_DOWN_COMPACT_FINE) ? kBM : kBM * kDownCG;
+}
 
 const char* spmlp_last_error(void) { return g_last_error.c_str(); }
 
@@ -982,6 +1015,20 @@ int spmlp_mask_decode(const void* data, int64_t n, uint32_t* tile_bits, int64_t 
 
 int spmlp_tile_bits_from_h(const void* h, uint32_t* tile_bits, int64_t T, int F, int dtype, void* stream) {
   return tile_bits_impl(h, tile_bits, T, F, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int spmlp_tile_bits16_words(int F) {
+  if (F <= 0) return 0;
+  return (F / 16 + 31) / 32;
+}
+
+int64_t spmlp_tile_bits16_size(int64_t T, int F) {
+  if (T <= 0 || F <= 0) return 0;
+  return ((T + kBitsRows - 1) / kBitsRows) * static_cast<int64_t>(spmlp_tile_bits16_words(F));
+}
+
+int spmlp_tile_bits16_from_h(const void* h, uint32_t* tile_bits16, int64_t T, int F, void* stream) {
+  return tile_bits16_impl(h, tile_bits16, T, F, static_cast<cudaStream_t>(stream));
 }
 
 int spmlp_up_gate(const void* x, const void* w_in, const void* b_in, void* h, uint32_t* tile_bits, void* z_out,

@@ -51,6 +51,9 @@ def tile_bits_size(tokens: int, features: int) -> int:
     return int(_lib.load().spmlp_tile_bits_size(tokens, features))
 
 
+_COMPACT_MODES = {"compact": _lib.DOWN_COMPACT, "compact_fine": _lib.DOWN_COMPACT_FINE}
+
+
 def _down_mode(skip: bool | str) -> int:
     if skip is False:
         return _lib.DOWN_DENSE
@@ -58,7 +61,16 @@ def _down_mode(skip: bool | str) -> int:
         return _lib.DOWN_SKIP
     if skip == "fine":
         return _lib.DOWN_SKIP_FINE
-    raise ValueError("skip must be True/'coarse', 'fine' or False")
+    if isinstance(skip, str) and skip in _COMPACT_MODES:
+        return _COMPACT_MODES[skip]
+    raise ValueError("skip must be True/'coarse', 'fine', 'compact', 'compact_fine' or False")
+
+
+def _bits_size(skip: bool | str, tokens: int, features: int) -> int:
+    """Words of the bitmap a down mode reads: 16x16 tiles for the compact modes, else 16x64."""
+    if isinstance(skip, str) and skip in _COMPACT_MODES:
+        return tile_bits16_size(tokens, features)
+    return tile_bits_size(tokens, features)
 
 
 def down_tile_tokens(skip: bool | str = True) -> int:
@@ -69,6 +81,23 @@ def down_tile_tokens(skip: bool | str = True) -> int:
 
 def tile_bits_words(features: int) -> int:
     return int(_lib.load().spmlp_tile_bits_words(features))
+
+
+def tile_bits16_size(tokens: int, features: int) -> int:
+    return int(_lib.load().spmlp_tile_bits16_size(tokens, features))
+
+
+def tile_bits16_from_h(h: torch.Tensor, bits: torch.Tensor | None = None) -> torch.Tensor:
+    """16x16 tile bitmap of h [T,F] (int32 words) for the compact down modes."""
+    device, dtype, code = _device_dtype(h)
+    _check("h", h, dtype, device)
+    t, f = h.shape
+    if bits is None:
+        bits = torch.empty((tile_bits16_size(t, f),), device=device, dtype=torch.int32)
+    _check("bits", bits, torch.int32, device, (tile_bits16_size(t, f),))
+    with torch.cuda.device(device):
+        _lib.call("spmlp_tile_bits16_from_h", _ptr(h), _ptr(bits), t, f, _stream(device))
+    return bits
 
 
 def tile_bits_from_h(h: torch.Tensor, bits: torch.Tensor | None = None) -> torch.Tensor:
@@ -241,7 +270,9 @@ def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor,
 
     h [T,F], w_out [d,F], b_out [d] or None, residual [T,d] or None.
     skip: True / "coarse" (256-token tiles on CTA pairs), "fine" (128-token tiles,
-    finer skipping for token-blocked zeros) or False (dense).
+    finer skipping for token-blocked zeros), "compact" / "compact_fine" (the same
+    tiles gathering only live 16-feature granules; ``bits`` is then the 16x16 bitmap
+    of ``tile_bits16_from_h``) or False (dense).
     stats: optional int64[2] device tensor accumulating issued / skipped K16 steps.
     """
     device, dtype, code = _device_dtype(h)
@@ -257,7 +288,7 @@ def down_sparse(h: torch.Tensor, bits: torch.Tensor | None, w_out: torch.Tensor,
     if mode != _lib.DOWN_DENSE:
         if bits is None:
             raise ValueError("skipping needs the tile bitmap")
-        _check("bits", bits, torch.int32, device, (tile_bits_size(t, f),))
+        _check("bits", bits, torch.int32, device, (_bits_size(skip, t, f),))
     if y is None:
         y = torch.empty((t, d), device=device, dtype=dtype)
     _check("y", y, dtype, device, (t, d))

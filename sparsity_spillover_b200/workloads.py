@@ -127,6 +127,20 @@ def tile_structured_h(tokens: int, features: int, p: float, seed: int, device, d
     return h, float(live.float().mean())
 
 
+def corner_tile_h(tokens: int, features: int, p: float, seed: int, device, dtype=torch.float16,
+                  tile_tokens: int = 8, tile_features: int = 16) -> tuple[torch.Tensor, float]:
+    """h with the structure of the reference's corner-tile gate (8-token x 16-feature tiles
+    kept or zeroed whole, runs/063-2026-10-07-pythia14m-tile-specialized-kernel/tile_gate.py:9-33):
+    each tile kept with probability p, GELU(N(0,1)) values inside.
+
+    Returns (h, kept tile fraction)."""
+    g = _gen(seed, device)
+    keep = torch.rand(-(-tokens // tile_tokens), features // tile_features, generator=g, device=device) < p
+    vals = torch.nn.functional.gelu(torch.randn(tokens, features, generator=g, device=device))
+    mask = keep.repeat_interleave(tile_tokens, 0)[:tokens].repeat_interleave(tile_features, 1)
+    return torch.where(mask, vals, torch.zeros((), device=device)).to(dtype), float(keep.float().mean())
+
+
 def zipf_active_tiles(n_tiles: int, fraction: float, seed: int, exponent: float = 1.1) -> np.ndarray:
     """Active 128-column vocabulary tiles for the tile-gated head.
 
