@@ -4,6 +4,7 @@
     python -m sparsity_spillover_b200.profile_case --case tile [--p 0.1] [--skip fine]
     python -m sparsity_spillover_b200.profile_case --case head [--d 128] [--frac 0.1] [--kappa K]
     python -m sparsity_spillover_b200.profile_case --case joint [--tokens 32768]
+    python -m sparsity_spillover_b200.profile_case --case corner [--tokens 32768] [--p 0.01] [--skip compact_fine]
 
 * ``mlp``  one cfg1 layer (d=512, F=2048, fp16, one-sided gate at 10% density):
            up_gate then down_sparse with the residual, ``iters`` times.
@@ -14,6 +15,9 @@
            ``--kappa`` the K-gated head (16x16 corner certificates of an fp32 N(0,1) input).
 * ``joint`` the joint consumer on a cfg1 layer: up_gate (identity, then gated) once,
            then the joint kernel ``iters`` times (h at 10% density, z ~ N(0,1)).
+* ``corner`` h with the reference's corner-tile structure (8-token x 16-feature tiles kept
+           with probability p, fp16, F=2048) through the down projection (d=512) in the
+           ``--skip`` mode (compact modes read the 16x16 bitmap).
 
 Inputs are seeded synthetic tensors; device memory stays well under 1 GB.
 """
@@ -28,13 +32,13 @@ from . import ops, workloads
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--case", choices=["mlp", "tile", "head", "joint"], default="mlp")
+    ap.add_argument("--case", choices=["mlp", "tile", "head", "joint", "corner"], default="mlp")
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--p", type=float, default=0.1)
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--frac", type=float, default=0.1)
-    ap.add_argument("--skip", choices=["coarse", "fine"], default="coarse")
+    ap.add_argument("--skip", choices=["coarse", "fine", "compact", "compact_fine"], default="coarse")
     ap.add_argument("--kappa", type=float, default=None, help="head: K gate with this threshold")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
@@ -62,6 +66,14 @@ def main() -> None:
                     continue
                 ops.up_gate(x, layer.w_in, layer.b_in, gate, h=h, bits=bits)
                 ops.down_sparse(h, bits, layer.w_out, layer.b_out, x, y=y)
+        elif args.case == "corner":
+            h, _ = workloads.corner_tile_h(args.tokens, 2048, args.p, seed=3, device=dev)
+            w = (torch.randn(512, 2048, device=dev) * 0.02).half()
+            compact = args.skip.startswith("compact")
+            bits = ops.tile_bits16_from_h(h) if compact else ops.tile_bits_from_h(h)
+            y = torch.empty(args.tokens, 512, dtype=torch.float16, device=dev)
+            for _ in range(args.iters):
+                ops.down_sparse(h, bits, w, None, skip=args.skip, y=y)
         elif args.case == "tile":
             h, _ = workloads.tile_structured_h(args.tokens, 2048, args.p, seed=3, device=dev)
             w = (torch.randn(512, 2048, device=dev) * 0.02).bfloat16()
