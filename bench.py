@@ -549,6 +549,11 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
     if sdist.multicast_available(device):
         fused_mc = sdist.FusedDffSplit(split, t_rank * world, multicast=True)
         runs.append(("dff_split_fused_multicast", lambda: fused_mc.forward(x_all, check=False)))
+    # the product's default form in token slices on their own streams, so that one slice's
+    # reduction over NVLink overlaps the next slice's projections
+    pipes = {n: sdist.PipelinedDffSplit(split, t_rank * world, parts=n) for n in (2, 4)}
+    for n, pipe in pipes.items():
+        runs.append((f"dff_split_pipelined{n}", lambda pipe=pipe: pipe.forward(x_all, check=False)))
     runs.append(("token_sharded", run_tokens))
     out = {}
     for name, fn in runs:
@@ -597,17 +602,31 @@ def dff_split_parity(runs, run_tokens, world: int, device, split, full, x_all, t
     if sdist.multicast_available(device):
         mc1 = sdist.FusedDffSplit(split[:1], t_rank * world, multicast=True)
         one.append(("dff_split_fused_multicast", lambda: mc1.forward(x_all, check=False)))
+    pipe1 = sdist.PipelinedDffSplit(split[:1], t_rank * world, parts=2)
+
+    def run_pipe1():
+        # rank r's blocks of the two slices, against the same tokens' rows of ref over all tokens
+        return torch.cat(pipe1.forward(x_all, check=False))
+
+    sub = t_rank // 2
+    ref1_pipe = torch.cat([ops.mlp_forward(xs, L0.w_in, L0.b_in, L0.w_out, L0.b_out, split[0].gate, residual=xs)
+                           for xs in (x_all[p * t_rank * world // 2 + rank * sub:p * t_rank * world // 2 + (rank + 1) * sub]
+                                      .contiguous() for p in range(2))])
     errs, names = [], []
     for name, fn in one:
         y = fn()
         torch.cuda.synchronize(device)
         errs.append(rel(y, ref1))
         names.append(name)
+    y = run_pipe1()
+    torch.cuda.synchronize(device)
+    errs.append(rel(y, ref1_pipe))
+    names.append("dff_split_pipelined2")
     # the chain
     ref = run_tokens().clone()
     chained = []
     for name, fn in runs:
-        if name == "token_sharded":
+        if name == "token_sharded" or name.startswith("dff_split_pipelined"):
             continue
         y = fn()
         torch.cuda.synchronize(device)
@@ -617,7 +636,8 @@ def dff_split_parity(runs, run_tokens, world: int, device, split, full, x_all, t
     dist.all_reduce(vec, op=dist.ReduceOp.MAX)
     vals = vec.cpu().tolist()
     res = {f"{n}_max_rel_err": vals[i] for i, n in enumerate(names)}
-    res.update({f"{n}_chained_max_rel_err": vals[len(names) + i] for i, n in enumerate(names)})
+    chained_names = [n for n in names if not n.startswith("dff_split_pipelined")]
+    res.update({f"{n}_chained_max_rel_err": vals[len(names) + i] for i, n in enumerate(chained_names)})
     res["reference"] = ("one layer: ops.mlp_forward of that layer on this rank's tokens on one GPU (fp16); chained: "
                         "the one-GPU chain of all the layers")
     res["tolerance"] = 2e-3

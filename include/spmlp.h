@@ -323,6 +323,13 @@ int spmlp_head_sparse(const void* x, const uint32_t* support, const void* w_voca
 int spmlp_head_fill(void* logits, const int32_t* tiles, int n_tiles, int64_t T, int V, int dtype,
                     float value, void* stream);
 
+/* At most `sms` SMs of the current device for the persistent GEMMs launched afterwards
+ * on it (0 = every SM, the default), like cuBLAS's cublasSetSmCountTarget: a caller that
+ * runs other kernels concurrently on another stream (the d_ff split's reduction over
+ * NVLink beside the next token slice's projections) leaves them SMs.  A CTA pair counts
+ * two.  No reference counterpart. */
+int spmlp_set_sm_count_target(int sms);
+
 /* Status word of `device` written by kernels that gave up on a bounded wait
  * (0 = none; otherwise the code of the most recent wait that gave up, which
  * stays until cleared).  Within one launch, the first wait that gives up makes

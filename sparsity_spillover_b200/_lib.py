@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "spmlp_head_prepare": (I32, [VP, VP, VP, I64, I32, I32, F32, VP]),
     "spmlp_head_sparse": (I32, [VP, VP, VP, VP, VP, I32, I64, I32, I32, I32, I32, VP, VP]),
     "spmlp_selftest_wait": (I32, [VP]),
+    "spmlp_set_sm_count_target": (I32, [I32]),
     "spmlp_device_status": (I32, [I32, _c.POINTER(I32)]),
     "spmlp_clear_device_status": (I32, [I32]),
 }

@@ -20,39 +20,63 @@ struct BroadcastTargets {
   int n;
 };
 
+// Vectors (8 elements, 16 bytes) each thread has in flight per pass of the grid-stride
+// loops below: the loads of kVecsInFlight vectors are issued before any is used, so
+// that a grid squeezed onto a few SMs (beside a persistent GEMM of another token
+// slice) still keeps enough NVLink / HBM requests outstanding.
+constexpr int kVecsInFlight = 4;
+
 template <bool BF16>
 __global__ void __launch_bounds__(256) reduce_broadcast_kernel(const uint16_t* __restrict__ recv, int world,
                                                                int64_t elems, int d, const uint16_t* __restrict__ bias,
                                                                const uint16_t* residual, BroadcastTargets targets) {
   using D = DType<BF16>;
+  constexpr int U = kVecsInFlight;
   const int64_t vecs = elems / 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < vecs;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < world; ++r) {
-      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(recv + r * elems) + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i0 < vecs; i0 += U * stride) {
+    float acc[U][8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] += D::lo(w[j]);
-        acc[2 * j + 1] += D::hi(w[j]);
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[u][e] = 0.f;
+    for (int r = 0; r < world; ++r) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = i0 + u * stride;
+        v[u] = i < vecs ? __ldcs(reinterpret_cast<const uint4*>(recv + r * elems) + i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[u][2 * j] += D::lo(w[j]);
+          acc[u][2 * j + 1] += D::hi(w[j]);
+        }
       }
     }
-    uint32_t out[4];
-    const int col = static_cast<int>((i * 8) % d);
-    uint4 b = make_uint4(0u, 0u, 0u, 0u);
-    if (bias != nullptr) b = __ldg(reinterpret_cast<const uint4*>(bias + col));
-    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(acc[2 * j] + D::lo(bw[j]), acc[2 * j + 1] + D::hi(bw[j]));
-    if (residual != nullptr) {
-      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
-      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= vecs) break;
+      uint32_t out[4];
+      const int col = static_cast<int>((i * 8) % d);
+      uint4 b = make_uint4(0u, 0u, 0u, 0u);
+      if (bias != nullptr) b = __ldg(reinterpret_cast<const uint4*>(bias + col));
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(rw[j]), D::hi(out[j]) + D::hi(rw[j]));
+      for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(acc[u][2 * j] + D::lo(bw[j]), acc[u][2 * j + 1] + D::hi(bw[j]));
+      if (residual != nullptr) {
+        const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(rw[j]), D::hi(out[j]) + D::hi(rw[j]));
+      }
+      const uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
+      for (int k = 0; k < targets.n; ++k) reinterpret_cast<uint4*>(targets.dst[k])[i] = o;
     }
-    const uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
-    for (int k = 0; k < targets.n; ++k) reinterpret_cast<uint4*>(targets.dst[k])[i] = o;
   }
   __threadfence_system();  // peer stores are performed before the kernel completes
 }
@@ -97,25 +121,36 @@ __global__ void __launch_bounds__(256) multicast_reduce_broadcast_kernel(const u
                                                                          const uint16_t* __restrict__ bias,
                                                                          const uint16_t* residual) {
   using D = DType<BF16>;
+  constexpr int U = kVecsInFlight;
   const int64_t vecs = elems / 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < vecs;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint4 sv = multimem_ld_reduce_add_v4<BF16>(mc_part + 8 * i);
-    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-    const int col = static_cast<int>((i * 8) % d);
-    uint4 b = make_uint4(0u, 0u, 0u, 0u);
-    if (bias != nullptr) b = __ldg(reinterpret_cast<const uint4*>(bias + col));
-    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-    uint32_t out[4];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i0 < vecs; i0 += U * stride) {
+    uint4 sv[U];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(sw[j]) + D::lo(bw[j]), D::hi(sw[j]) + D::hi(bw[j]));
-    if (residual != nullptr) {
-      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
-      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(rw[j]), D::hi(out[j]) + D::hi(rw[j]));
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < vecs) sv[u] = multimem_ld_reduce_add_v4<BF16>(mc_part + 8 * i);
     }
-    multimem_st_v4<BF16>(mc_x + 8 * i, make_uint4(out[0], out[1], out[2], out[3]));
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= vecs) break;
+      const uint32_t sw[4] = {sv[u].x, sv[u].y, sv[u].z, sv[u].w};
+      const int col = static_cast<int>((i * 8) % d);
+      uint4 b = make_uint4(0u, 0u, 0u, 0u);
+      if (bias != nullptr) b = __ldg(reinterpret_cast<const uint4*>(bias + col));
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+      uint32_t out[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(sw[j]) + D::lo(bw[j]), D::hi(sw[j]) + D::hi(bw[j]));
+      if (residual != nullptr) {
+        const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[j] = D::pack_rn(D::lo(out[j]) + D::lo(rw[j]), D::hi(out[j]) + D::hi(rw[j]));
+      }
+      multimem_st_v4<BF16>(mc_x + 8 * i, make_uint4(out[0], out[1], out[2], out[3]));
+    }
   }
   __threadfence_system();  // the multicast stores are performed before the kernel completes
 }

@@ -76,6 +76,7 @@ constexpr int kJointFineStages = 4, kJointFineEpiWarps = 4;
 
 struct DeviceInfo {
   int sm_count = 0;
+  int sm_target = 0;    // spmlp_set_sm_count_target: SMs the persistent GEMMs may use (0 = all)
   int* status = nullptr;
   void* ctx = nullptr;  // the context the cached addresses belong to
   bool ok = false;
@@ -241,6 +242,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     }
     units = max_clusters[dev_id];
   }
+  // A caller that runs other kernels beside the GEMMs (a reduction over NVLink on another
+  // stream) leaves them SMs by capping the persistent grid.
+  if (dev->sm_target > 0) units = std::min(units, std::max(1, dev->sm_target / CG));
   // The last round of the persistent grid: when it would leave at least half of the
   // units idle, its tiles run as two half-width items each (the down projection and
   // the joint consumer, whose epilogue warps write through an output ring).
@@ -1155,6 +1159,15 @@ int spmlp_selftest_wait(void* stream) {
   wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev->status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wait_probe_kernel launch");
+  return 0;
+}
+
+int spmlp_set_sm_count_target(int sms) {
+  if (sms < 0) return fail(SPMLP_EINVAL, "sms=%d must be >= 0 (0 = every SM)", sms);
+  DeviceInfo* dev = nullptr;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  dev->sm_target = sms;
   return 0;
 }
 

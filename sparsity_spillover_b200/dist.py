@@ -276,31 +276,126 @@ class FusedDffSplit:
         incomplete.  With ``check`` (default) the call waits for its kernels and raises
         ``PeerTimeoutError`` when the device status word reports such a failure; pass
         ``check=False`` inside timed loops and read ``ops.device_status`` afterwards."""
-        from . import ops
+        self.begin(x)
+        for i in range(len(self.layers)):
+            self.layer_step(i)
+        return self.finish(check)
 
+    # The forward in steps, so that several instances (token slices) can interleave their
+    # launches on their own streams (PipelinedDffSplit).  Every step launches on the
+    # current stream.
+    def begin(self, x: torch.Tensor) -> None:
         if tuple(x.shape) != (self.tokens, self.d):
             raise ValueError(f"x must be [{self.tokens}, {self.d}]")
         # The previous call ended with a barrier after every rank's last broadcast, so
         # overwriting X here races with no other rank.
         self.x.copy_(x)
+
+    def layer_step(self, i: int) -> None:
+        self.layer_gemms(i)
+        self.layer_exchange(i)
+
+    def layer_gemms(self, i: int) -> None:
+        """Layer i's up_gate and (scattering) down projection: tensor-bound, local."""
+        from . import ops
+
+        layer = self.layers[i]
+        ops.up_gate(self.x, layer.w_in, layer.b_in, layer.gate, h=self.h, bits=self.bits)
+        if self.multicast:
+            ops.down_sparse(self.h, self.bits, layer.w_out, None, None, skip=self.skip, y=self.part)
+        else:
+            ops.down_scatter(self.h, self.bits, layer.w_out, self.slots, skip=self.skip)
+
+    def layer_exchange(self, i: int) -> None:
+        """Layer i's barrier, reduction + broadcast and barrier: NVLink-bound, few SMs."""
+        from . import ops
+
+        layer = self.layers[i]
         mine = self.x[self.rank * self.rows:(self.rank + 1) * self.rows]
-        for layer in self.layers:
-            ops.up_gate(self.x, layer.w_in, layer.b_in, layer.gate, h=self.h, bits=self.bits)
-            if self.multicast:
-                ops.down_sparse(self.h, self.bits, layer.w_out, None, None, skip=self.skip, y=self.part)
-                self._barrier()
-                ops.reduce_broadcast_multicast(self.mc_part, self.mc_x, self.rows, self.d, layer.b_out, mine,
-                                               self.dtype, self.device)
-            else:
-                ops.down_scatter(self.h, self.bits, layer.w_out, self.slots, skip=self.skip)
-                self._barrier()
-                ops.reduce_broadcast(self.recv, layer.b_out, mine, self.targets)
-            self._barrier()
+        self._barrier()
+        if self.multicast:
+            ops.reduce_broadcast_multicast(self.mc_part, self.mc_x, self.rows, self.d, layer.b_out, mine,
+                                           self.dtype, self.device)
+        else:
+            ops.reduce_broadcast(self.recv, layer.b_out, mine, self.targets)
+        self._barrier()
+
+    def finish(self, check: bool = True) -> torch.Tensor:
+        from . import ops
+
+        mine = self.x[self.rank * self.rows:(self.rank + 1) * self.rows]
         if check:
             status = ops.device_status(self.device.index)
             if status != 0:
                 raise PeerTimeoutError(self.rank, status)
         return mine
+
+
+class PipelinedDffSplit:
+    """The fused d_ff split over ``parts`` token slices, each a FusedDffSplit with its own
+    buffers and barrier flags, launched layer by layer on its own CUDA stream, so that one
+    slice's exchange (barrier, reduction + broadcast over NVLink: bandwidth-bound, few SMs)
+    runs while the next slice's up and down projections (tensor-bound) run on the other SMs.
+
+    The projections of all slices form one chain across the streams (slice p's projections
+    of layer i start after slice p-1's, slice 0's of layer i+1 after the last slice's of
+    layer i): run side by side they would only share the tensor cores and reach their
+    exchanges together, with nothing left to overlap them.  The persistent GEMMs are
+    capped at ``gemm_sms`` SMs (ops.set_sm_count_target; default: all but 16) during the
+    forward, so that the exchange kernels always find SMs; 0 leaves them uncapped.  Slice
+    p holds tokens [p T/parts, (p+1) T/parts); rank r's output is its block of every slice.
+    A barrier waits only on the same slice's barrier of the other ranks, and every wait
+    across ranks points to an earlier (layer, slice) step, so the launches cannot wait on
+    one another in a cycle."""
+
+    def __init__(self, layers: list[DffSplitMLP], tokens: int, *, parts: int = 2, gemm_sms: int | None = None,
+                 skip: bool | str = True, multicast: bool | None = None):
+        if parts < 1 or tokens % parts:
+            raise ValueError(f"T={tokens} must split into {parts} equal token slices")
+        self.parts = [FusedDffSplit(layers, tokens // parts, skip=skip, multicast=multicast) for _ in range(parts)]
+        first = self.parts[0]
+        self.device, self.tokens, self.d = first.device, tokens, first.d
+        self.world, self.rank = first.world, first.rank
+        props = torch.cuda.get_device_properties(self.device)
+        self.gemm_sms = props.multi_processor_count - 16 if gemm_sms is None else int(gemm_sms)
+        self.streams = [torch.cuda.Stream(self.device) for _ in range(parts)]
+        self.multicast = first.multicast
+
+    def forward(self, x: torch.Tensor, *, check: bool = True) -> list[torch.Tensor]:
+        """x [T, d] (the same on every rank) -> this rank's output block of each slice
+        (``parts`` tensors of [T / parts / world, d])."""
+        from . import ops
+
+        if tuple(x.shape) != (self.tokens, self.d):
+            raise ValueError(f"x must be [{self.tokens}, {self.d}]")
+        n = len(self.parts)
+        rows = self.tokens // n
+        main = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(main)
+        ops.set_sm_count_target(self.gemm_sms, self.device.index)
+        try:
+            for p, (part, st) in enumerate(zip(self.parts, self.streams)):
+                st.wait_event(start)
+                with torch.cuda.stream(st):
+                    part.begin(x[p * rows:(p + 1) * rows])
+            gemms_done = None
+            for i in range(len(self.parts[0].layers)):
+                for part, st in zip(self.parts, self.streams):
+                    with torch.cuda.stream(st):
+                        if gemms_done is not None:
+                            st.wait_event(gemms_done)
+                        part.layer_gemms(i)
+                        gemms_done = torch.cuda.Event()
+                        gemms_done.record(st)
+                        part.layer_exchange(i)
+            for st in self.streams:
+                ev = torch.cuda.Event()
+                ev.record(st)
+                main.wait_event(ev)
+        finally:
+            ops.set_sm_count_target(0, self.device.index)
+        return [part.finish(check) for part in self.parts]
 
 
 class PeerTimeoutError(RuntimeError):

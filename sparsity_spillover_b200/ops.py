@@ -527,6 +527,13 @@ def head_fill(logits: torch.Tensor, tiles: torch.Tensor, value: float) -> torch.
     return logits
 
 
+def set_sm_count_target(sms: int, device: int | None = None) -> None:
+    """Cap the persistent GEMMs launched afterwards on ``device`` at ``sms`` SMs (0 = all)."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    with torch.cuda.device(dev):
+        _lib.call("spmlp_set_sm_count_target", int(sms))
+
+
 def device_status(device: int | None = None) -> int:
     """Status word written by kernels that gave up on a bounded wait (0 = none)."""
     dev = torch.cuda.current_device() if device is None else int(device)

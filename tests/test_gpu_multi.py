@@ -68,6 +68,16 @@ def _worker(rank, world, port, queue):
         y_fused = fused.forward(x)
         err_fused = omlp.max_rel_error(y_fused.float().cpu(), ref[lo:hi].float().cpu())
         full_x = fused.x.clone()
+        # The same layers as two token slices on two streams (PipelinedDffSplit): each rank's
+        # block of each slice equals the unsliced fused split's rows (peer form: the
+        # reduction sums in rank order in both).
+        pipe = sdist.PipelinedDffSplit(layers, t, parts=2, multicast=False)
+        blocks = pipe.forward(x)
+        half, sub = t // 2, t // 2 // world
+        pipe_rows = [full_x[p * half + rank * sub:p * half + (rank + 1) * sub] for p in range(2)]
+        pipe_same = all(bool(torch.equal(b, r)) for b, r in zip(blocks, pipe_rows))
+        pipe_err = max(omlp.max_rel_error(b.float().cpu(), ref[p * half + rank * sub:p * half + (rank + 1) * sub]
+                                          .float().cpu()) for p, b in enumerate(blocks))
         y_again = fused.forward(x).clone()  # a second call reuses the buffers and gives the same result
         same_again = bool(torch.equal(y_again, y_fused)) and bool(torch.equal(fused.x, full_x))
         rows_ok = omlp.max_rel_error(full_x.float().cpu(), ref.float().cpu())  # every block reached every rank
@@ -93,7 +103,8 @@ def _worker(rank, world, port, queue):
             except sdist.PeerTimeoutError as exc:
                 raised = exc.code == 6
             ops.clear_device_status(rank)
-        queue.put((rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable and raised, err1))
+        queue.put((rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable and raised, err1,
+                   pipe_err, pipe_same))
     finally:
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
@@ -112,7 +123,8 @@ def test_dff_split_over_nccl_and_token_shards():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable, err1 in results:
+    for (rank, err, same, status, err_fused, same_again, rows_ok, timeout_status, usable, err1,
+         pipe_err, pipe_same) in results:
         assert err1 <= 2e-3, (rank, err1)  # one layer, NCCL and fused forms
         assert err <= 2e-2, (rank, err)  # fp16 partials summed by NCCL, then bias and residual rounding
         assert same
@@ -121,6 +133,8 @@ def test_dff_split_over_nccl_and_token_shards():
         assert same_again
         assert rows_ok <= 2e-2, (rank, rows_ok)
         assert timeout_status == 6 and usable  # SPMLP_STATUS_TIMEOUT_PEER
+        assert pipe_err <= 2e-2, (rank, pipe_err)
+        assert pipe_same  # per token, the sliced run computes exactly what the unsliced one does
 
 
 def _multicast_worker(rank, world, port, queue):
