@@ -554,12 +554,26 @@ def dff_split_measure(device, world: int, rank: int, layers: int = 4, steps: int
     pipes = {n: sdist.PipelinedDffSplit(split, t_rank * world, parts=n) for n in (2, 4)}
     for n, pipe in pipes.items():
         runs.append((f"dff_split_pipelined{n}", lambda pipe=pipe: pipe.forward(x_all, check=False)))
+    # the exchange alone and the projections alone, which bound the pipelined forms
+    form = fused_mc if fused_mc is not None and world >= sdist.FusedDffSplit.MULTICAST_MIN_WORLD else fused_peer
+
+    def exchanges_only():
+        for i in range(layers):
+            form.layer_exchange(i)
+
+    def projections_only():
+        for i in range(layers):
+            form.layer_gemms(i)
     runs.append(("token_sharded", run_tokens))
     out = {}
-    for name, fn in runs:
+    for name, fn in runs + [("dff_split_exchanges_only", exchanges_only),
+                            ("dff_split_projections_only", projections_only)]:
         fn()
         dist.barrier(device_ids=[device.index])
         t = max_over_ranks(time_device(fn, steps, device), world, device)
+        if name.endswith("_only"):
+            out[f"{name}_ms_per_step"] = t * 1e3
+            continue
         out[f"{name}_tokens_per_s"] = world * t_rank / t
         out[f"{name}_ms_per_step"] = t * 1e3
     # the product's default choice at this world size (FusedDffSplit(multicast=None))
@@ -602,16 +616,17 @@ def dff_split_parity(runs, run_tokens, world: int, device, split, full, x_all, t
     if sdist.multicast_available(device):
         mc1 = sdist.FusedDffSplit(split[:1], t_rank * world, multicast=True)
         one.append(("dff_split_fused_multicast", lambda: mc1.forward(x_all, check=False)))
-    pipe1 = sdist.PipelinedDffSplit(split[:1], t_rank * world, parts=2)
+    parts = 4
+    pipe1 = sdist.PipelinedDffSplit(split[:1], t_rank * world, parts=parts)
 
     def run_pipe1():
-        # rank r's blocks of the two slices, against the same tokens' rows of ref over all tokens
+        # rank r's blocks of the slices, against the same tokens' rows of ref over all tokens
         return torch.cat(pipe1.forward(x_all, check=False))
 
-    sub = t_rank // 2
+    sub, span = t_rank // parts, t_rank * world // parts
     ref1_pipe = torch.cat([ops.mlp_forward(xs, L0.w_in, L0.b_in, L0.w_out, L0.b_out, split[0].gate, residual=xs)
-                           for xs in (x_all[p * t_rank * world // 2 + rank * sub:p * t_rank * world // 2 + (rank + 1) * sub]
-                                      .contiguous() for p in range(2))])
+                           for xs in (x_all[p * span + rank * sub:p * span + (rank + 1) * sub].contiguous()
+                                      for p in range(parts))])
     errs, names = [], []
     for name, fn in one:
         y = fn()
@@ -621,7 +636,7 @@ def dff_split_parity(runs, run_tokens, world: int, device, split, full, x_all, t
     y = run_pipe1()
     torch.cuda.synchronize(device)
     errs.append(rel(y, ref1_pipe))
-    names.append("dff_split_pipelined2")
+    names.append(f"dff_split_pipelined{parts}")
     # the chain
     ref = run_tokens().clone()
     chained = []
@@ -797,8 +812,15 @@ def summarize(line: dict) -> dict:
         out["host_link_gbs"] = [r(hl["h2d_gbs"], 1), r(hl["d2h_gbs"], 1), r(hl["concurrent_gbs_each_way"], 1)]
     ds = line.get("dff_split_cfg3")
     if isinstance(ds, dict) and "parity" in ds:
-        out["dff_split_mtok_s"] = {k[len("dff_split"):].strip("_") or "nccl": r(v / 1e6, 2)
-                                   for k, v in ds.items() if k.endswith("tokens_per_s")}
+        def form(k):
+            k = k[:-len("_tokens_per_s")]
+            return k[len("dff_split"):].strip("_") or "nccl" if k.startswith("dff_split") else k
+
+        out["dff_split_mtok_s"] = {form(k): r(v / 1e6, 2) for k, v in ds.items() if k.endswith("_tokens_per_s")}
+        nccl = ds.get("dff_split_tokens_per_s")
+        best = max((v, k) for k, v in ds.items() if k.startswith("dff_split_") and k.endswith("_tokens_per_s"))
+        if nccl:
+            out["dff_split_best_vs_nccl"] = [form(best[1]), r(best[0] / nccl)]
         out["dff_split_parity"] = {k: (round(v, 6) if isinstance(v, float) else v)
                                    for k, v in ds["parity"].items() if k != "reference"}
     out["value_mtok_s"] = r(line["value"] / 1e6, 2)

@@ -68,16 +68,15 @@ def _worker(rank, world, port, queue):
         y_fused = fused.forward(x)
         err_fused = omlp.max_rel_error(y_fused.float().cpu(), ref[lo:hi].float().cpu())
         full_x = fused.x.clone()
-        # The same layers as two token slices on two streams (PipelinedDffSplit): each rank's
-        # block of each slice equals the unsliced fused split's rows (peer form: the
+        # The same layers as four token slices on four streams (PipelinedDffSplit): each
+        # rank's block of each slice equals the unsliced fused split's rows (peer form: the
         # reduction sums in rank order in both).
-        pipe = sdist.PipelinedDffSplit(layers, t, parts=2, multicast=False)
+        pipe = sdist.PipelinedDffSplit(layers, t, parts=4, multicast=False)
         blocks = pipe.forward(x)
-        half, sub = t // 2, t // 2 // world
-        pipe_rows = [full_x[p * half + rank * sub:p * half + (rank + 1) * sub] for p in range(2)]
-        pipe_same = all(bool(torch.equal(b, r)) for b, r in zip(blocks, pipe_rows))
-        pipe_err = max(omlp.max_rel_error(b.float().cpu(), ref[p * half + rank * sub:p * half + (rank + 1) * sub]
-                                          .float().cpu()) for p, b in enumerate(blocks))
+        span, sub = t // 4, t // 4 // world
+        rows_of = [slice(p * span + rank * sub, p * span + (rank + 1) * sub) for p in range(4)]
+        pipe_same = all(bool(torch.equal(b, full_x[sl])) for b, sl in zip(blocks, rows_of))
+        pipe_err = max(omlp.max_rel_error(b.float().cpu(), ref[sl].float().cpu()) for b, sl in zip(blocks, rows_of))
         y_again = fused.forward(x).clone()  # a second call reuses the buffers and gives the same result
         same_again = bool(torch.equal(y_again, y_fused)) and bool(torch.equal(fused.x, full_x))
         rows_ok = omlp.max_rel_error(full_x.float().cpu(), ref.float().cpu())  # every block reached every rank
@@ -178,8 +177,14 @@ def _multicast_worker(rank, world, port, queue):
             ref1 = ops.mlp_forward(x, full[0].w_in, full[0].b_in, full[0].w_out, full[0].b_out, gate, residual=x)
             mc1 = sdist.FusedDffSplit(layers[:1], t, multicast=True)
             err1 = omlp.max_rel_error(mc1.forward(x).float().cpu(), ref1[lo:hi].float().cpu())
+            # the same layer as four token slices on four streams, projections capped
+            pipe1 = sdist.PipelinedDffSplit(layers[:1], t, parts=4, multicast=True)
+            span, sub = t // 4, t // 4 // world
+            rows_of = [slice(p * span + rank * sub, p * span + (rank + 1) * sub) for p in range(4)]
+            err1_pipe = max(omlp.max_rel_error(b.float().cpu(), ref1[sl].float().cpu())
+                            for b, sl in zip(pipe1.forward(x), rows_of))
             torch.cuda.synchronize(dev)
-            result.update(multicast=mc.multicast, err1=err1,
+            result.update(multicast=mc.multicast and pipe1.multicast, err1=max(err1, err1_pipe),
                           err=omlp.max_rel_error(y.float().cpu(), ref[lo:hi].float().cpu()),
                           rows_ok=omlp.max_rel_error(full_x.float().cpu(), ref.float().cpu()),
                           same_again=bool(torch.equal(y, y2)),
