@@ -60,6 +60,7 @@ def test_argument_errors_are_reported_without_a_gpu(lib):
     assert rc == -1 and b"tile_bits" in lib.spmlp_last_error()
     rc = lib.spmlp_up_gate(16, 16, None, 16, 16, None, 64, 128, 512, 0, 6, k, 12, None)
     assert rc == -2  # corner gate: T=64 is not a multiple of seq_len=12
+    assert lib.spmlp_set_sm_count_target(-1) == -1 and b"sms" in lib.spmlp_last_error()
 
 
 def test_joint_and_gate_argument_errors_without_a_gpu(lib):
