@@ -278,8 +278,8 @@ int spmlp_mlp_forward(const void* x, const void* w_in, const void* b_in, const v
  * The first call on each device looks up the buffer's device address
  * (cudaGetSymbolAddress with that device current) and caches it; make that
  * first call before any stream capture.  Every call on a device shares the one
- * buffer, which keeps the last call's contents (the bitmap is cleared on each
- * call): calls that can overlap on the GPU — on different streams or from
+ * buffer, which keeps the last call's contents (every bit of the bitmap is
+ * rewritten on each call): calls that can overlap on the GPU — on different streams or from
  * different host threads, on the same device — race on it and must be
  * serialised by the caller.  Arguments and results are as spmlp_mlp_forward's. */
 #define SPMLP_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)

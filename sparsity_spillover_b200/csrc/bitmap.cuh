@@ -40,20 +40,6 @@ __global__ void __launch_bounds__(256) tile_bits_kernel(const uint16_t* __restri
   for (int w = threadIdx.x; w < words; w += blockDim.x) bits[static_cast<size_t>(rg) * words + w] = s_words[w];
 }
 
-// Clears the up projection's bitmap before its kernel ORs into it.  Launched as a
-// programmatic dependent of the previous kernel in the stream (a reader of the same
-// buffer, e.g. the previous layer's down projection): it lets the up projection
-// start its set-up at once, and waits for the previous kernel to finish before it
-// writes.  The up projection's own grid_dependency_wait then orders its ORs after
-// these stores.  A memset node in its place would break that chain of overlaps.
-__global__ void __launch_bounds__(256) zero_words_kernel(uint32_t* __restrict__ p, int64_t n) {
-  grid_launch_dependents();
-  grid_dependency_wait();
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    p[i] = 0u;
-}
-
 // Elementwise gate of an activation x [T, F] into out (which may alias x), and
 // optionally the 16x64 tile bitmap of the gated values.  Gates: identity, one-
 // sided (keep z >= kappa), symmetric (keep |z| >= kappa), ReLU -- the same packed

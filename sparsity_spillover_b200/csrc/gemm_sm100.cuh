@@ -1209,17 +1209,31 @@ __global__ void __launch_bounds__(GemmTraits<KIND, BN, STAGES, BF16, EPI, CG, RI
         }
       }
       if constexpr (KIND == KIND_UP) {
-        // Publish this warp's 16x64 bits: two 16-row groups per warp quarter.
-        if (lane == 0 && nz_bits != 0) {
+        // Publish this warp's 16x64 bits: two 16-row groups per warp quarter.  Every bit
+        // of the bitmap belongs to exactly one warp (its 64 columns, its 16 rows), which
+        // writes it whether set or clear: an AND clears the warp's dead groups and an OR
+        // sets its live ones, so the buffer needs no clearing before the launch and
+        // whatever it held is overwritten.
+        if (lane == 0) {
           const int g0 = n_col0 / kBitsCols;  // first 64-column group of the tile
           const int word = g0 >> 5;
           const int shift = g0 & 31;          // BN/64 <= 4 groups stay inside one word
+          const int row_groups = (p.M + kBitsRows - 1) / kBitsRows;
+          uint32_t own = 0;                   // this warp's groups (two 32-column chunks each)
+          for (int grp = ch_begin >> 1; grp < (ch_end >> 1); ++grp)
+            if (n_col0 + grp * kBitsCols < p.N) own |= 1u << (shift + grp);
+          // The owner of the last 64-column group also clears the unused bits above it.
+          const int g_last = p.N / kBitsCols - 1;
+          if ((g_last >> 5) == word && ((own >> (g_last & 31)) & 1u)) own |= ~((2u << (g_last & 31)) - 1u);
           for (int half = 0; half < 2; ++half) {
+            const int rg = (row0 >> 4) + half;
+            if (rg >= row_groups || own == 0) continue;
             uint32_t w = 0;
             for (int grp = 0; grp < BN / kBitsCols; ++grp)
               if ((nz_bits >> (2 * grp + half)) & 1u) w |= 1u << (shift + grp);
-            const int rg = (row0 >> 4) + half;
-            if (w != 0) atomicOr(p.bits_out + static_cast<size_t>(rg) * p.bits_words + word, w);
+            uint32_t* wp = p.bits_out + static_cast<size_t>(rg) * p.bits_words + word;
+            if (w != own) atomicAnd(wp, ~own | w);
+            if (w != 0) atomicOr(wp, w);
           }
         }
       }

@@ -357,22 +357,8 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   CUtensorMap tc;
   if ((rc = make_out_map(&tc, h, T, F, bf16))) return rc;
   const int words = spmlp_tile_bits_words(F);
-  const int64_t bits_size = spmlp_tile_bits_size(T, F);
+  // No clear of tile_bits first: the kernel writes every bit of it, set or clear.
   cudaError_t e;
-  {  // clear the bitmap (a programmatic dependent launch, see zero_words_kernel)
-    cudaLaunchConfig_t zc = {};
-    cudaLaunchAttribute za[1];
-    za[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    za[0].val.programmaticStreamSerializationAllowed = kProgrammaticLaunch;
-    const int64_t blocks = (bits_size + 255) / 256;
-    zc.gridDim = dim3(static_cast<unsigned>(blocks < dev->sm_count ? blocks : dev->sm_count));
-    zc.blockDim = dim3(256);
-    zc.stream = stream;
-    zc.attrs = za;
-    zc.numAttrs = 1;
-    e = cudaLaunchKernelEx(&zc, zero_words_kernel, bits, bits_size);
-    if (e != cudaSuccess) return cuda_fail(e, "clearing tile_bits");
-  }
   GemmParams p{};
   p.M = static_cast<int>(T);
   p.N = F;
@@ -877,8 +863,8 @@ int mlp_forward_noalloc_impl(const void* x, const void* w_in, const void* b_in, 
   if (rc) return rc;
   void* h = scratch;
   uint32_t* bits = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(scratch) + h_bytes);
-  // up_gate clears the bitmap (zero_words_kernel) before its kernel ORs into it,
-  // so nothing the previous call left in the buffer is read.
+  // up_gate writes every bit of the bitmap, set or clear, so nothing the previous
+  // call left in the buffer is read.
   rc = up_gate_impl(x, w_in, b_in, h, bits, nullptr, T, d, F, dtype, gate_op, kappa, seq_len, stream);
   if (rc) return rc;
   return down_impl(h, bits, w_out, b_out, residual, y, T, F, d, dtype, mode, stats, stream);

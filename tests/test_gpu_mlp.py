@@ -105,6 +105,36 @@ def test_up_gate_matches_reference_gate_on_kernel_z(dtype, op, shape):
             assert float((zf - k).abs().max()) <= 2 * og.ulp(k, dtype)
 
 
+@pytest.mark.parametrize("fill", [0xFFFFFFFF, "random"])
+@pytest.mark.parametrize("t,d,f,density", [(1000, 128, 320, 0.002), (4096, 512, 2048, 0.0005), (300, 256, 1024, 0.1)])
+def test_up_gate_rewrites_every_bitmap_bit(fill, t, d, f, density):
+    """The up projection writes each bit of the bitmap set or clear (no clear launch
+    before it): a buffer full of stale bits comes out equal to the oracle's bitmap, with
+    dead 64-column groups, a partial last 16-row group, a partial last tile and unused
+    bits above the last group of a word."""
+    from sparsity_spillover_b200 import ops
+
+    dtype = torch.float16
+    x, w_in, b_in, _, _ = _inputs(t, d, f, dtype, seed=t + f)
+    spec = _spec(og.ONE_SIDED, _kappa(x, w_in, b_in, density, dtype))
+    xd, wd, bd = _cuda(x, w_in, b_in)
+    n = ops.tile_bits_size(t, f)
+    if fill == "random":
+        g = torch.Generator().manual_seed(t)
+        bits = torch.randint(-2**31, 2**31 - 1, (n,), generator=g, dtype=torch.int64).to(torch.int32).to(DEV)
+    else:
+        bits = torch.full((n,), -1, dtype=torch.int32, device=DEV)
+    h = torch.empty(t, f, dtype=dtype, device=DEV)
+    ops.up_gate(xd, wd, bd, spec, h=h, bits=bits)
+    torch.cuda.synchronize()
+    ref = obit.tile_bits(h.cpu())
+    np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), ref)
+    live = obit.tile_mask(h.cpu())
+    assert live.any()
+    if density < 0.01:
+        assert not live.all()  # dead groups too: their stale bits were cleared
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("density", [1.0, 0.25, 0.1, 0.02])
 @pytest.mark.parametrize("skip", [True, "fine"])
