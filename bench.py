@@ -1038,8 +1038,8 @@ def run_ours(args):
         "e2e": {"value": world * t / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": t * d * 2,
                 "d2h_bytes_per_step": t * d * 2, "pipelining": "batches: H2D(i+1) and D2H(i-1) overlap compute(i)",
                 "matches_device_forward": e2e_ok, "ms_per_step": t_e2e * 1e3},
-        "gpu_launches": args.steps * nl * 3,
-        "execution": "value: CUDA-graph replay of the 6-layer step (18 kernels per step: bitmap clear, up_gate, "
+        "gpu_launches": args.steps * nl * 2,
+        "execution": "value: CUDA-graph replay of the 6-layer step (12 kernels per step: up_gate and "
                      "down_sparse per layer, chained by programmatic dependent launch); "
                      "roofline: eager steps with per-kernel CUDA events",
         "clocks": clocks,
