@@ -80,3 +80,12 @@ def test_partition_helpers():
     assert sdist.dff_slice(4096, 8, 3) == (1536, 2048)
     with pytest.raises(ValueError):
         sdist.dff_slice(4096, 3, 0)
+
+
+def test_pipelined_dff_split_rejects_uneven_slices():
+    """Token slices must be equal: checked before any buffer or collective is set up."""
+    from sparsity_spillover_b200 import dist as sdist
+
+    for tokens, parts in ((1000, 3), (1024, 0)):
+        with pytest.raises(ValueError):
+            sdist.PipelinedDffSplit([], tokens, parts=parts)
