@@ -61,7 +61,7 @@ extern "C" {
 #define SPMLP_DOWN_SKIP_FINE 2 /* as SPMLP_DOWN_SKIP with 128-token tiles on single
                               CTAs: skips more K-blocks when zeros come in token
                               blocks narrower than 256 (e.g. 64-token tiles)        */
-#define SPMLP_DOWN_COMPACT 3 /* compact mode (the survey's "mode 2 compact"): the bitmap
+#define SPMLP_DOWN_COMPACT 3 /* compact mode: live K granules gathered; the bitmap
                               is the 16x16 one (spmlp_tile_bits16_from_h); each
                               pipeline stage gathers four live 16-feature granules of
                               the tile (the union over its tokens) into shared memory,
