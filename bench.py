@@ -35,7 +35,7 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes per launch from one ncu capture of the same layer shape
 # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/gemm_up_down_cfg1.md).
-NCU_TRAFFIC_BYTES: dict[str, float | None] = {"up_gate": 117.1e6, "down_sparse": 188.4e6}
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {"up_gate": 116.4e6, "down_sparse": 192.0e6}
 
 
 def peaks() -> tuple[dict, str]:
