@@ -31,6 +31,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "gated-MLP fwd tokens/s at 1/2/4/8 B200 and speedup vs dense GEMM by density"
 DENSITY = 0.10
+WORKLOAD = ("cfg1: Pythia-70M gated MLP, 6 stacked layers, d=512 F=2048, T=32768/GPU, "
+            "one-sided threshold gate at 10% element density, residual chained")
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes per launch from one ncu capture of the same layer shape
@@ -1017,9 +1019,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded N(0,1) x, GPT-NeoX init weights)",
-        "config": {"workload": "cfg1: Pythia-70M gated MLP, 6 stacked layers, d=512 F=2048, T=32768/GPU, "
-                               "one-sided threshold gate at 10% element density, residual chained",
-                   "tokens_per_gpu": t, "layers": nl, "density_target": DENSITY,
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": t, "layers": nl, "density_target": DENSITY,
                    "density_measured": stack.density, "parallelism": f"token-sharded x{world}",
                    "l2": "working set per step > L2 (h alone is 134 MB per layer)"},
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
@@ -1093,8 +1093,9 @@ def run_reference(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 2048 / value * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded N(0,1) x, GPT-NeoX init weights)",
-        "config": {"workload": "cfg1 sample: Pythia-70M gated MLP, 6 layers, d=512 F=2048, 2048-token sample, "
-                               "one-sided threshold gate at 10% density (reference CPU path, oracle port)"},
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": cfg.tokens, "layers": cfg.layers,
+                   "density_target": DENSITY, "parallelism": "host cores (the reference's CPU path, oracle port)",
+                   "sample": "each step times a 2048-token sample of this workload"},
         "impl": "reference",
         "cpu_baseline": {"kind": base["kind"], "cores": base["cores"], "sample": base["sample"], "value": value,
                          "unit": "tokens/s"},
