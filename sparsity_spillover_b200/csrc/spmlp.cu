@@ -48,12 +48,17 @@ constexpr int kProgrammaticLaunch = 1;  // GEMM launches overlap the previous ke
 
 // Tile configuration of the up-projection: pipeline stages, epilogue warps,
 // CTAs per tile, output ring slots per epilogue warp (0 = whole-tile slab).
-constexpr int kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
+constexpr int kUpBN = 256, kUpStages = 4, kUpEpiWarps = 8, kUpCG = 2, kUpRing = 0;
+// Up-projection with few tiles (e.g. the 14M shape): 128 x 128 tiles on single CTAs.
+constexpr int kUpSmallBN = 128;
 // Down-projection, dense and coarse-skip modes: 256-token tiles on CTA pairs.
 // Its long reduction (K = d_ff) leaves the epilogue idle most of the time, so
 // four epilogue warps and a two-slot output ring suffice, and the shared memory
 // goes to six operand stages (the loads of h are the bound).
 constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
+// Down-projection with d <= 128 (the 14M shape): 128-column tiles on the pairs; each
+// stage is 16 KiB of h and 8 KiB of W_out per CTA, so eight stages fit.
+constexpr int kDownNarrowBN = 128, kDownNarrowStages = 8;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
 constexpr int kDownFineBN = 256, kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
 // Vocabulary head: 128 x 128 tiles on single CTAs.
@@ -269,10 +274,10 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 
 // Up-projection launch with the gate operator (and the folded LayerNorm) as
 // compile-time parameters.
-template <int BN, int G>
+template <int BN, int G, bool SMALL>
 int launch_up_gate(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
                    bool bf16, bool ln, cudaStream_t stream, DeviceInfo* dev) {
-  constexpr int S = kUpStages, E = kUpEpiWarps, C = kUpCG, R = kUpRing;
+  constexpr int S = kUpStages, E = kUpEpiWarps, C = SMALL ? 1 : kUpCG, R = kUpRing;
   if (ln)
     return bf16 ? launch_gemm<KIND_UP, G, BN, S, true, E, C, R, true>(ta, tb, tc, p, stream, dev)
                 : launch_gemm<KIND_UP, G, BN, S, false, E, C, R, true>(ta, tb, tc, p, stream, dev);
@@ -280,13 +285,13 @@ int launch_up_gate(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
               : launch_gemm<KIND_UP, G, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev);
 }
 
-template <int BN>
+template <int BN, bool SMALL>
 int launch_up(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p, int gate_op,
               bool bf16, cudaStream_t stream, DeviceInfo* dev) {
   const bool ln = p.ln_c != nullptr;
 #define SPMLP_UP_CASE(G) \
   case G:                \
-    return launch_up_gate<BN, G>(ta, tb, tc, p, bf16, ln, stream, dev);
+    return launch_up_gate<BN, G, SMALL>(ta, tb, tc, p, bf16, ln, stream, dev);
   switch (gate_op) {
     SPMLP_UP_CASE(GATE_IDENTITY)
     SPMLP_UP_CASE(GATE_GELU)
@@ -350,10 +355,15 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   DeviceInfo* dev = nullptr;
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
-  constexpr int BN = 256;
+  // Few tiles (fewer 256 x 256 pair tiles than CTA pairs): 128 x 128 tiles on single CTAs,
+  // so that more SMs share the work and each epilogue warp handles half as many chunks.
+  const int64_t pair_tiles = ((T + 2 * kBM - 1) / (2 * kBM)) * ((F + kUpBN - 1) / kUpBN);
+  const bool small = pair_tiles * kUpCG <= dev->sm_count;
+  const int bn = small ? kUpSmallBN : kUpBN;
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
-  if ((rc = make_kmajor_map(&tb, w_in, F, d, BN / kUpCG, bf16))) return rc;
+  // B rows per CTA: kUpBN / kUpCG on a pair, kUpSmallBN on one CTA (both 128).
+  if ((rc = make_kmajor_map(&tb, w_in, F, d, small ? kUpSmallBN : kUpBN / kUpCG, bf16))) return rc;
   CUtensorMap tc;
   if ((rc = make_out_map(&tc, h, T, F, bf16))) return rc;
   const int words = spmlp_tile_bits_words(F);
@@ -363,7 +373,7 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   p.M = static_cast<int>(T);
   p.N = F;
   p.K = d;
-  p.n_tiles = (F + BN - 1) / BN;
+  p.n_tiles = (F + bn - 1) / bn;
   p.bias = ln ? nullptr : b_in;
   p.ln_s = ln_s;
   p.ln_c = ln_c;
@@ -380,7 +390,9 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   // block's corner row may belong to another tile, so the up projection writes the
   // ungated z and corner_gate_kernel gates it in place and rebuilds the bitmap.
   const bool corner_pass = gate_op == SPMLP_GATE_CORNER && seq_len != T && seq_len % 8 != 0;
-  rc = launch_up<BN>(ta, tb, tc, p, corner_pass ? SPMLP_GATE_IDENTITY : gate_op, bf16, stream, dev);
+  const int op = corner_pass ? SPMLP_GATE_IDENTITY : gate_op;
+  rc = small ? launch_up<kUpSmallBN, true>(ta, tb, tc, p, op, bf16, stream, dev)
+             : launch_up<kUpBN, false>(ta, tb, tc, p, op, bf16, stream, dev);
   if (rc || !corner_pass) return rc;
   const int groups = static_cast<int>((T + kBitsRows - 1) / kBitsRows);
   const size_t smem = static_cast<size_t>(words) * 4;
@@ -427,7 +439,10 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   const bool bf16 = dtype == SPMLP_BF16;
   constexpr int BN = 256, BNF = kDownFineBN;
   const bool fine = mode == SPMLP_DOWN_SKIP_FINE || mode == SPMLP_DOWN_COMPACT_FINE;
-  const int bn = fine ? BNF : BN;
+  // d <= 128 on CTA pairs (the dense and 256-token skip modes): 128-column tiles, so that no
+  // MMA runs on the empty half of a 256-column tile.  Same token tile, same skip accounting.
+  const bool narrow = !fine && !compact && slots == nullptr && d <= kDownNarrowBN;
+  const int bn = fine ? BNF : (narrow ? kDownNarrowBN : BN);
   const int box_k = compact ? 16 : kBK;  // compact: gathered K16 granules, 32-byte swizzle
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, h, T, F, kBM, bf16, box_k))) return rc;
@@ -469,6 +484,11 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
   if (fine) {
     if (bf16) return launch_gemm<KIND_DOWN, 0, BNF, SF, true, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
     return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+  }
+  if (narrow) {
+    constexpr int BNN = kDownNarrowBN, SN = kDownNarrowStages;
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BNN, SN, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+    return launch_gemm<KIND_DOWN, 0, BNN, SN, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
   }
   if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
   return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);

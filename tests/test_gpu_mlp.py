@@ -314,6 +314,35 @@ def test_cfg3_shape_up_gate_and_down_sparse(dtype, skip):
     assert stats.cpu().tolist() == [issued, skipped]
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("t,d,f,density", [(4096, 128, 512, 0.1), (1000, 128, 512, 0.01), (25600, 128, 512, 0.002)])
+def test_small_shapes_take_narrow_tiles(dtype, t, d, f, density):
+    """The 14M shape (d=128, F=512): the up projection runs 128 x 128 tiles on single CTAs
+    when its pair tiles would not fill the GPU, and the down projection 128-column tiles
+    on CTA pairs (T=25600: 100 pair tiles, the last round split into half-width items).  h, the bitmap, y and the skip counters are held to the same bars as
+    the large shapes; the skipping y equals the dense y bit for bit."""
+    from sparsity_spillover_b200 import ops
+
+    x, w_in, b_in, w_out, b_out = _inputs(t, d, f, dtype, seed=14 + t)
+    spec = _spec(og.ONE_SIDED, _kappa(x, w_in, b_in, density, dtype))
+    xd, wd, bd, wod, bod = _cuda(x, w_in, b_in, w_out, b_out)
+    r = torch.randn(t, d, generator=torch.Generator().manual_seed(15)).to(dtype)
+    z = torch.empty(t, f, dtype=dtype, device=DEV)
+    h, bits = ops.up_gate(xd, wd, bd, spec, z_out=z)
+    stats = torch.zeros(2, dtype=torch.int64, device=DEV)
+    y = ops.down_sparse(h, bits, wod, bod, r.to(DEV), skip=True, stats=stats)
+    y_dense = ops.down_sparse(h, None, wod, bod, r.to(DEV), skip=False)
+    torch.cuda.synchronize()
+    z_c, h_c = z.cpu(), h.cpu()
+    assert omlp.max_rel_error(z_c, omlp.linear(x, w_in, b_in)) <= TOL[dtype]
+    assert torch.equal(h_c, og.apply(z_c, og.ONE_SIDED, spec.kappa_for(dtype)))
+    np.testing.assert_array_equal(bits.cpu().numpy().view(np.uint32), obit.tile_bits(h_c))
+    assert torch.equal(y, y_dense)
+    assert omlp.max_rel_error(y.cpu(), omlp.down_from_h(h_c, w_out, b_out, residual=r, dtype=dtype)) <= TOL[dtype]
+    issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=1, m_tile=ops.down_tile_tokens(True))
+    assert stats.cpu().tolist() == [issued, skipped]
+
+
 @pytest.mark.parametrize("skip", [True, "fine"])
 def test_cfg2_full_size_tile_structured(skip):
     """cfg2 at its full size (T=65536, d=512, F=2048, bf16, 64x64 tiles live with p=0.1):
