@@ -57,8 +57,9 @@ constexpr int kUpSmallBN = 128;
 // goes to six operand stages (the loads of h are the bound).
 constexpr int kDownStages = 6, kDownEpiWarps = 4, kDownCG = 2, kDownRing = 2;
 // Down-projection with d <= 128 (the 14M shape): 128-column tiles on the pairs; each
-// stage is 16 KiB of h and 8 KiB of W_out per CTA, so eight stages fit.
-constexpr int kDownNarrowBN = 128, kDownNarrowStages = 8;
+// stage is 16 KiB of h and 8 KiB of W_out per CTA.  Eight epilogue warps (two chunks each:
+// few tiles, so the epilogue is on the critical path) and seven stages fit.
+constexpr int kDownNarrowBN = 128, kDownNarrowStages = 7, kDownNarrowEpiWarps = 8;
 // Down-projection, fine-skip mode: 128-token tiles on single CTAs.
 constexpr int kDownFineBN = 256, kDownFineStages = 4, kDownFineEpiWarps = 4, kDownFineRing = 2;
 // Vocabulary head: 128 x 128 tiles on single CTAs.
@@ -486,9 +487,9 @@ int down_impl(const void* h, const uint32_t* bits, const void* w_out, const void
     return launch_gemm<KIND_DOWN, 0, BNF, SF, false, EF, 1, RF>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
   }
   if (narrow) {
-    constexpr int BNN = kDownNarrowBN, SN = kDownNarrowStages;
-    if (bf16) return launch_gemm<KIND_DOWN, 0, BNN, SN, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
-    return launch_gemm<KIND_DOWN, 0, BNN, SN, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+    constexpr int BNN = kDownNarrowBN, SN = kDownNarrowStages, EN = kDownNarrowEpiWarps;
+    if (bf16) return launch_gemm<KIND_DOWN, 0, BNN, SN, true, EN, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
+    return launch_gemm<KIND_DOWN, 0, BNN, SN, false, EN, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
   }
   if (bf16) return launch_gemm<KIND_DOWN, 0, BN, S, true, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
   return launch_gemm<KIND_DOWN, 0, BN, S, false, E, C, R>(ta, tb, tc, p, stream, dev, trp, &ta, &tb, &tb_half);
