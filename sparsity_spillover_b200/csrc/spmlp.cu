@@ -356,10 +356,15 @@ int up_gate_impl(const void* x, const void* w_in, const void* b_in, void* h, uin
   DeviceInfo* dev = nullptr;
   if ((rc = current_device_info(&dev))) return rc;
   const bool bf16 = dtype == SPMLP_BF16;
-  // Few tiles (fewer 256 x 256 pair tiles than CTA pairs): 128 x 128 tiles on single CTAs,
-  // so that more SMs share the work and each epilogue warp handles half as many chunks.
+  // Few tiles: 128 x 128 tiles on single CTAs, so that more SMs share the work and each
+  // epilogue warp handles half as many chunks.  Chosen when those tiles fit in one round of
+  // the SMs, or when K <= 128 and the 256 x 256 pair tiles would not fill the CTA pairs.
+  // Measured (fp16, us per launch, pair / small): T x d x F = 4096x128x512 6.7 / 4.9,
+  // 8192x128x512 7.3 / 6.6, 16384x128x512 10.1 / 10.3, 1024x512x2048 8.6 / 7.2,
+  // 2048x512x2048 9.4 / 10.7, 4096x512x2048 13.1 / 17.2, 2048x256x1024 7.3 / 5.6.
   const int64_t pair_tiles = ((T + 2 * kBM - 1) / (2 * kBM)) * ((F + kUpBN - 1) / kUpBN);
-  const bool small = pair_tiles * kUpCG <= dev->sm_count;
+  const int64_t small_tiles = ((T + kBM - 1) / kBM) * ((F + kUpSmallBN - 1) / kUpSmallBN);
+  const bool small = small_tiles <= dev->sm_count || (d <= 128 && pair_tiles * kUpCG <= dev->sm_count);
   const int bn = small ? kUpSmallBN : kUpBN;
   CUtensorMap ta, tb;
   if ((rc = make_kmajor_map(&ta, x, T, d, kBM, bf16))) return rc;
