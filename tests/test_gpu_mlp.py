@@ -526,3 +526,32 @@ def test_last_round_split_tiles_match_the_oracle(skip):
     assert omlp.max_rel_error(y.cpu()[tail], y_ref) <= TOL[torch.bfloat16]
     issued, skipped = obit.skip_counts(obit.tile_mask(h_c), f, n_tiles=d // 256, m_tile=ops.down_tile_tokens(skip))
     assert stats.cpu().tolist() == [issued, skipped]
+
+
+@pytest.mark.parametrize("sms", [2, 9, 100])
+def test_sm_count_target_keeps_results_bit_identical(sms):
+    """With the persistent GEMMs capped at a few SMs (as the pipelined d_ff split does while
+    another stream's exchange runs), up_gate and every down mode give the same bits as
+    uncapped; the cap is reset afterwards."""
+    from sparsity_spillover_b200 import ops
+
+    dtype, t, d, f = torch.float16, 2000, 512, 2048
+    x, w_in, b_in, w_out, b_out = _inputs(t, d, f, dtype, seed=sms)
+    spec = _spec(og.ONE_SIDED, _kappa(x, w_in, b_in, 0.1, dtype))
+    xd, wd, bd, wod, bod = _cuda(x, w_in, b_in, w_out, b_out)
+
+    def run():
+        h, bits = ops.up_gate(xd, wd, bd, spec)
+        ys = [ops.down_sparse(h, bits, wod, bod, xd, skip=s) for s in (False, True, "fine")]
+        torch.cuda.synchronize()
+        return [h, bits] + ys
+
+    ref = run()
+    try:
+        ops.set_sm_count_target(sms)
+        capped = run()
+    finally:
+        ops.set_sm_count_target(0)
+    for a, b in zip(ref, capped):
+        assert torch.equal(a, b)
+    assert ops.device_status() == 0
